@@ -1,0 +1,190 @@
+"""Pin the CPU oracle against golden vectors produced by the reference itself.
+
+The fixtures in ``tests/golden`` were written by ``tests/golden/make_golden.py``
+running the reference's own code (``prefix_attention_forward``,
+``tree_attention_forward``, ``verify_new``, ``PagedKVCache``, ``ChunkArena``,
+``BundleScheduler``, ``FusedBundleVerifier``).  Every oracle function must
+reproduce them: bit-exact for integer results, and within float rounding for
+the fp32 attention path.
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import torch
+
+from conftest import bf16_from_bits, load_golden
+from oracle import acceptance, arena, attention, bundles, paged
+
+
+def _t(x, dtype):
+    if dtype == "bf16":
+        return torch.from_numpy(bf16_from_bits(x)).to(torch.bfloat16)
+    return torch.from_numpy(np.asarray(x))
+
+
+def test_attention_fp32_matches_reference():
+    z = load_golden("attn_fp32.npz")
+    q, kp, vp, kt, vt = (_t(z[k], "f32") for k in ("q", "k_prefix", "v_prefix", "k_tree", "v_tree"))
+    keep = torch.from_numpy(z["keep"])
+    g = q.shape[2] // kp.shape[1]
+    kpe = attention.repeat_kv(kp, g).transpose(1, 2)
+    vpe = attention.repeat_kv(vp, g).transpose(1, 2)
+    kte = attention.repeat_kv(kt, g).transpose(1, 2)
+    vte = attention.repeat_kv(vt, g).transpose(1, 2)
+    p_out, p_lse = attention.prefix_attention(q, kpe, vpe)
+    assert torch.allclose(p_out, _t(z["prefix_out"], "f32"), atol=1e-6, rtol=1e-5)
+    assert torch.allclose(p_lse, torch.from_numpy(z["prefix_lse"]), atol=1e-5, rtol=1e-6)
+    b, m = q.shape[:2]
+    t_out, w = attention.tree_attention(q, kte, vte, keep[None].expand(b, -1, -1), p_lse)
+    assert torch.allclose(t_out, _t(z["tree_out"], "f32"), atol=1e-6, rtol=1e-5)
+    assert torch.allclose(w, _t(z["weight"], "f32"), atol=1e-6, rtol=1e-5)
+    merged = attention.merge(t_out, p_out, w)
+    assert torch.allclose(merged, _t(z["merged"], "f32"), atol=1e-6, rtol=1e-5)
+    # The whole-layer helper and the single-softmax precision anchor agree.
+    assert torch.allclose(attention.reference_verify_layer(q, kp, vp, kt, vt, keep), merged, atol=1e-6)
+    full_k = torch.cat([kp, kt], dim=2)
+    full_v = torch.cat([vp, vt], dim=2)
+    anchor, _ = attention.full_masked_attention(q, full_k, full_v, keep, kp.shape[2])
+    assert torch.allclose(anchor, merged, atol=2e-6, rtol=1e-4)
+
+
+def test_attention_bf16_matches_reference_bitwise():
+    z = load_golden("attn_bf16.npz")
+    q, kp, vp, kt, vt = (_t(z[k], "bf16") for k in ("q", "k_prefix", "v_prefix", "k_tree", "v_tree"))
+    keep = torch.from_numpy(z["keep"])
+    merged = attention.reference_verify_layer(q, kp, vp, kt, vt, keep)
+    ref = _t(z["merged"], "bf16")
+    # Same torch ops on the same CPU: identical bits.
+    assert torch.equal(merged, ref)
+    # The reference's bf16 path (bf16 softmax weights, bf16 merge weight) is
+    # NOT within 2e-2 rel / 1e-3 abs of the fp32 anchor everywhere (about 3%
+    # of elements miss it, max abs error ~5e-3); the anchor rounded once to
+    # bf16 is.  The GPU kernels are therefore held to the fp32 anchor.
+    anchor, _ = attention.full_masked_attention(q, torch.cat([kp, kt], 2), torch.cat([vp, vt], 2), keep,
+                                                kp.shape[2])
+    err = (ref.float() - anchor).abs()
+    assert err.max() < 1e-2
+    assert torch.allclose(anchor.to(torch.bfloat16).float(), anchor, atol=1e-3, rtol=2e-2)
+
+
+def test_float_mask_roundtrip():
+    z = load_golden("attn_fp32.npz")
+    keep = torch.from_numpy(z["keep"])
+    fm = attention.float_mask_from_keep(keep, 7)
+    assert fm.shape == (1, 1, keep.shape[0], 7 + keep.shape[0])
+    assert torch.equal(attention.keep_from_float_mask(fm, keep.shape[0])[0], keep)
+
+
+def test_greedy_acceptance_matches_reference():
+    z = load_golden("accept_greedy.npz")
+    md = int(z["max_depth"])
+    for c in range(6):
+        g = lambda k: z[f"c{c}__{k}"]
+        logits = bf16_from_bits(g("logits"))
+        res = acceptance.accept_greedy(logits, g("draft"), g("parent"), g("pos"), md)
+        assert res["best_candidate"] == list(g("best_candidate")), c
+        assert res["accept_length"] == int(g("accept_length")), c
+        assert res["next_token"] == int(g("next_token")), c
+        kv = g("kv_in").copy()
+        new_len = acceptance.compact_contiguous([kv], int(g("cur_len")), len(g("draft")), res["path"])
+        assert new_len == int(g("new_len")), c
+        assert np.array_equal(kv, g("kv_out")), c
+
+
+def test_sampled_acceptance_matches_reference():
+    z = load_golden("accept_sample.npz")
+    md = int(z["max_depth"])
+    cases = sorted({k.split("__")[0] for k in z.files if "__" in k})
+    assert len(cases) >= 4
+    for c in cases:
+        g = lambda k: z[f"{c}__{k}"]
+        res = acceptance.accept_from_next(g("sampled"), g("draft"), g("parent"), g("pos"), md)
+        assert res["best_candidate"] == list(g("best_candidate")), c
+        assert res["accept_length"] == int(g("accept_length")), c
+        assert res["next_token"] == int(g("next_token")), c
+        kv = g("kv_in").copy()
+        acceptance.compact_contiguous([kv], int(g("cur_len")), len(g("draft")), res["path"])
+        assert np.array_equal(kv, g("kv_out")), c
+
+
+def test_argmax_nan_and_ties():
+    x = np.array([[1.0, 3.0, 3.0, 2.0], [np.nan, 5.0, np.nan, 1.0], [-np.inf, -np.inf, -np.inf, -np.inf]],
+                 dtype=np.float32)
+    assert list(acceptance.argmax_rows(x)) == list(torch.argmax(torch.from_numpy(x).to(torch.bfloat16),
+                                                                dim=-1).numpy())
+
+
+def test_paged_oracle_matches_reference():
+    z = load_golden("paged.npz")
+    log = json.loads(str(z["log"]))
+    pool_ref = z["pool"]
+    o = paged.PagedOracle(num_layers=2, num_heads=2, head_dim=8, page_size=4, max_pages=24)
+    gen = torch.Generator().manual_seed(3)
+    o.allocate(0, 22)
+    for t in range(22):
+        for layer in range(2):
+            o.write_row(0, layer, t, torch.randn(2, 8, generator=gen).numpy(), torch.randn(2, 8, generator=gen).numpy())
+    assert o.physical_blocks(0) == log[0][1]
+    o.fork(0, 1, 22)
+    assert o.physical_blocks(1) == log[1][1]
+    o.compact_path(1, int(z["compact_start"]), list(z["compact_path"]))
+    assert o.physical_blocks(1) == log[2][1]
+    for layer in range(2):
+        o.write_row(0, layer, 25, torch.randn(2, 8, generator=gen).numpy(), torch.randn(2, 8, generator=gen).numpy())
+    assert o.physical_blocks(0) == log[3][1]
+    o.free(1)
+    o.allocate(2, 7)
+    assert o.physical_blocks(2) == log[4][1]
+    assert np.array_equal(o.pool, pool_ref)
+    assert np.array_equal(o.ref, z["ref"])
+    assert sorted(o.free_pages) == list(z["free"])
+
+
+def test_arena_oracle_matches_reference():
+    z = load_golden("arena.npz")
+    states = json.loads(str(z["states"]))
+    a = arena.ArenaOracle(max_chunks=6, chunk_size=8, num_layers=2, num_heads=2, head_dim=4)
+    full = [(z["full_k"][i], z["full_v"][i]) for i in range(2)]
+    for st in states[:-1]:
+        view = a.update(st["req"], full)
+        assert {str(k): v for k, v in a.chunk_to_offset.items()} == st["mapping"]
+        assert a.active == st["active"] and a.free == st["free"]
+        assert view.shape[4] == st["view_len"]
+    assert np.array_equal(a.arena, z["arena_pre"])
+    a.compact()
+    assert {str(k): v for k, v in a.chunk_to_offset.items()} == states[-1]["mapping"]
+    assert np.array_equal(a.arena, z["arena_post"])
+
+
+def test_bundle_oracle_matches_reference():
+    cases = json.loads((load_golden.__globals__["GOLDEN"] / "bundles.json").read_text())
+    for c in cases:
+        pm = {i: p for i, p in enumerate(c["parent"])}
+        depth = {int(k): v for k, v in c["depth"].items()}
+        got = bundles.schedule(c["leaves"], pm, depth, c["bundle_size"], c["max_bundles"])
+        assert got == c["bundles"]
+
+
+def test_bundle_attention_oracle_matches_reference():
+    z = load_golden("bundle_verify.npz")
+    q, k, v = (torch.from_numpy(z[x]) for x in ("q", "k", "v"))
+    mask = torch.from_numpy(z["masks"][0])[None].expand(q.shape[0], -1, -1)
+    o, lse = attention.bundle_attention(q, k, v, mask)
+    assert torch.allclose(o, torch.from_numpy(z["out"]), atol=1e-6, rtol=1e-5)
+    assert torch.allclose(lse, torch.from_numpy(z["lse"]), atol=1e-5)
+
+
+def test_lse_merge_equals_full_softmax():
+    gen = torch.Generator().manual_seed(0)
+    q = torch.randn(1, 5, 4, 16, generator=gen)
+    k = torch.randn(1, 2, 40, 16, generator=gen)
+    v = torch.randn(1, 2, 40, 16, generator=gen)
+    full, full_lse = attention.full_masked_attention(q, k, v, None, 40)
+    parts = [attention.full_masked_attention(q, k[:, :, a:b], v[:, :, a:b], None, b - a)
+             for a, b in ((0, 7), (7, 30), (30, 40))]
+    o, l = attention.lse_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]))
+    assert torch.allclose(o, full, atol=1e-5)
+    assert torch.allclose(l, full_lse, atol=1e-5)
