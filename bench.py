@@ -1,0 +1,393 @@
+#!/usr/bin/env python3
+"""Benchmark: tree-verify attention on B200 (BASELINE config 2 and the sharded scaling run).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload auto|config2|sharded]
+
+A step is one verify-attention pass of one layer over the config-2 problem:
+64K-token paged KV cache (16-token pages, seeded random page permutation),
+a 64-node depth-8 draft tree, Llama-3.1-8B attention shapes (32 query / 8 KV
+heads, head_dim 128), bf16.  Steps rotate over 4 independent layer pools
+(1 GiB of KV in all) so no step finds the previous step's KV in the 126 MB L2.
+
+N = 1 runs config 2 on one GPU.  N > 1 (torchrun, one rank per GPU) runs the
+same 64K problem sequence-sharded: each rank attends its contiguous share of
+the pages, and one NCCL all_gather of the packed (O, lse) partials plus a
+local log-sum-exp merge gives every rank the full result ("scaling":
+"strong": total work fixed).  Time = max over ranks of CUDA-event time.
+
+`value` = algorithmic bytes (every visible K/V row once + Q/O/LSE/page
+table/bitmask) / step time, in GB/s, whole job.  `e2e` measures the same call
+through the public Python API with the per-step inputs (queries, tree mask)
+copied from pinned host memory and the result (output + LSE) read back to
+the host inside the timed region; the KV cache is device-resident state.
+
+--impl reference times the reference's own CPU path (prefix attention + tree
+attention + merge on repeat_kv-expanded K/V, fp32, restated in oracle/) on the
+host cores over a bounded sample of the same problem.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "specdiff-ae_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "tree-verify attn HBM GB/s (%peak) + verified tok/s @64K ctx, 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+# dram__bytes_read.sum + dram__bytes_write.sum per verify call (both kernels),
+# from the ncu capture summarised in profiles/attn_config2_ncu.md; None until
+# a capture of the current kernels exists.
+NCU_TRAFFIC_BYTES = None
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def physical_gpu_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [x.strip() for x in vis.split(",") if x.strip()]
+    if local < len(ids) and ids[local].isdigit():
+        return int(ids[local])
+    return local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[2:6]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def build_problems(rotate: int, dev, seed: int = 0):
+    from specverify import workloads as wl
+    probs = [wl.paged_verify(seed=seed + 100 * i, device=dev) for i in range(rotate)]
+    return probs
+
+
+def run_ours(args, rank, world, dev):
+    from specverify.runtime import attention, pack_tree_mask, verify_attention
+    from specverify.runtime import sharded as sh
+
+    rotate = 4
+    probs = build_problems(rotate, dev)
+    p0 = probs[0]
+    bits = [pack_tree_mask(p.tree.keep.to(dev)) for p in probs]
+    alg_bytes = p0.algorithmic_bytes()
+    flops = p0.flops()
+    m = p0.tree.rows
+    page = p0.page_size
+
+    if world == 1:
+        outs = [torch.empty_like(p.q) for p in probs]
+        lses = [torch.empty(p.q.shape[:3], dtype=torch.float32, device=dev) for p in probs]
+
+        def step(i):
+            p = probs[i % rotate]
+            attention(p.q, p.k_pool, p.v_pool, num_keys=p.num_keys, page_table=p.page_table,
+                      mask_bits=bits[i % rotate], mask_len=m, out=outs[i % rotate], lse=lses[i % rotate])
+        launches_per_step = 2
+        workload = "config2: paged tree verify, S=65536, 64-node depth-8 tree, 1 layer, bf16, B=1"
+    else:
+        # Sequence-sharded: this rank's share of the prefix pages; the last rank
+        # also holds the tree's pages and applies the tree bitmask.
+        verifier = sh.SequenceShardedVerify()
+        n_pages_prefix = p0.prefix_len // page
+        lo, hi = sh.shard_bounds(n_pages_prefix, world, rank)
+        shards = []
+        for p in probs:
+            tbl = p.page_table[:, lo:hi]
+            if rank == world - 1:
+                tbl = torch.cat([tbl, p.page_table[:, n_pages_prefix:]], dim=1)
+            shards.append(tbl.contiguous())
+        shard_len = (hi - lo) * page + (m if rank == world - 1 else 0)
+
+        def step(i):
+            p = probs[i % rotate]
+            verifier(p.q, p.k_pool, p.v_pool, shard_len, bits[i % rotate] if rank == world - 1 else None,
+                     page_table=shards[i % rotate])
+        launches_per_step = 3
+        workload = (f"config2 sequence-sharded over {world} GPUs: S=65536 paged, 64-node depth-8 tree, 1 layer, "
+                    f"bf16, one NCCL all_gather of (O, lse) partials + LSE merge per step")
+
+    # correctness spot check of the timed configuration (rank 0 vs single-GPU call)
+    for _ in range(args.warmup):
+        for i in range(rotate):
+            step(i)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(physical_gpu_index(torch.cuda.current_device()))
+    if rank == 0:
+        sampler.start()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        step(i)
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # ---- end to end through the public API with host buffers -------------
+    e2e = None
+    if world == 1 and not args.no_e2e:
+        q_host = [p.q.cpu().pin_memory() for p in probs]
+        keep_host = [p.tree.keep.clone().pin_memory() for p in probs]
+        out_host = [torch.empty(p.q.shape, dtype=p.q.dtype).pin_memory() for p in probs]
+        lse_host = [torch.empty(p.q.shape[:3], dtype=torch.float32).pin_memory() for p in probs]
+
+        def e2e_step(i):
+            p = probs[i % rotate]
+            q = q_host[i % rotate].to(dev, non_blocking=True)
+            keep = keep_host[i % rotate].to(dev, non_blocking=True)
+            o, lse = verify_attention(q, p.k_pool, p.v_pool, p.prefix_len, keep, page_table=p.page_table,
+                                      return_lse=True)
+            out_host[i % rotate].copy_(o, non_blocking=True)
+            lse_host[i % rotate].copy_(lse, non_blocking=True)
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        for i in range(args.steps):
+            e2e_step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1e3 / args.steps
+        ems = max(e0.elapsed_time(e1) / args.steps, wall)
+        h2d = p0.q.numel() * p0.q.element_size() + p0.tree.keep.numel()
+        d2h = p0.q.numel() * p0.q.element_size() + p0.q.shape[0] * p0.q.shape[1] * p0.q.shape[2] * 4
+        e2e = {"value": round(alg_bytes / (ems * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ems, 4),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "specverify.runtime.verify_attention (pinned host q/mask in, out/lse back to host)"}
+
+    total_bytes = alg_bytes  # whole job: the full 64K problem once per step (sharded or not)
+    value = total_bytes / (ms * 1e-3) / 1e9
+    hbm, kind = peaks()
+    per_gpu_peak = hbm
+    achieved_per_gpu = value / world
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) K/V, RoPE'd N(0,1)/sqrt(128) queries, random page permutation)",
+        "config": {
+            "workload": workload,
+            "context": p0.prefix_len, "tree_nodes": m, "heads": p0.q.shape[2], "kv_heads": p0.k_pool.shape[1],
+            "head_dim": p0.q.shape[3], "page_size": page, "layers_rotated": rotate,
+            "l2": "inputs larger than L2: 4 independent 268 MB KV pools rotated per step",
+            "algorithmic_bytes_per_step": alg_bytes, "flops_per_step": flops,
+            "parallelism": "single GPU" if world == 1 else f"sequence-sharded x{world}",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved_per_gpu, 1),
+            "peak": per_gpu_peak,
+            "unit": "GB/s",
+            "frac": round(achieved_per_gpu / per_gpu_peak, 4),
+            "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6.65 TB/s",
+            "traffic": NCU_TRAFFIC_BYTES,
+            "kernel": "verify attention (split-KV attention kernel + LSE merge kernel) per launch pair",
+            "tensor_tflops": round(flops / (ms * 1e-3) / 1e12 / world, 1),
+        },
+        "gpu_launches": launches_per_step * args.steps,
+        "e2e": e2e,
+        "clocks": clocks,
+    }
+    return result
+
+
+# ---------------------------------------------------------------------------
+# reference CPU path (oracle restatement), bounded sample
+# ---------------------------------------------------------------------------
+
+def cpu_reference_sample(sample_prefix: int, seed: int = 0, reps: int = 1):
+    """Time the reference's CPU verify pipeline (fp32, repeat_kv-expanded,
+    pages gathered by index_select) on the config-2 problem with the prefix
+    truncated to ``sample_prefix`` tokens.  Returns (GB/s of algorithmic
+    bytes of the sample, seconds per pass, threads, description)."""
+    from oracle import attention as oatt
+    from specverify import workloads as wl
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = wl.paged_verify(prefix_len=sample_prefix, device="cpu", dtype=torch.float32, seed=seed, spare_pages=0)
+    k, v = w.contiguous_kv(0)                                    # index_select through the page table
+    kk = k.permute(1, 0, 2)[None]
+    vv = v.permute(1, 0, 2)[None]
+    s = w.prefix_len
+    keep = w.tree.keep
+    oatt.reference_verify_layer(w.q, kk[:, :, :s], vv[:, :, :s], kk[:, :, s:], vv[:, :, s:], keep)  # warm
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        pages = w.page_table[0].long()
+        k2 = w.k_pool.index_select(0, pages).permute(1, 0, 2, 3).reshape(w.k_pool.shape[1], -1, w.k_pool.shape[3])
+        v2 = w.v_pool.index_select(0, pages).permute(1, 0, 2, 3).reshape(w.v_pool.shape[1], -1, w.v_pool.shape[3])
+        k2, v2 = k2[None, :, : w.num_keys], v2[None, :, : w.num_keys]
+        oatt.reference_verify_layer(w.q, k2[:, :, :s], v2[:, :, :s], k2[:, :, s:], v2[:, :, s:], keep)
+        best = min(best, time.perf_counter() - t0)
+    # algorithmic bytes of the sample counted at bf16 like the GPU problem
+    b, m, h, d = w.q.shape
+    alg = (s + m) * w.k_pool.shape[1] * d * 2 * 2 + 2 * m * h * d * 2 + m * h * 4 + w.page_table.numel() * 4
+    desc = (f"reference CPU path (prefix_attention_forward + tree_attention_forward + merge, repeat_kv, fp32, "
+            f"pages gathered by index_select) on config 2 with the prefix cut to {sample_prefix} tokens")
+    return alg / best / 1e9, best, torch.get_num_threads(), desc
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    sample = 8192
+    vals = []
+    for i in range(args.warmup + args.steps):
+        gbs, sec, thr, desc = cpu_reference_sample(sample, seed=i)
+        if i >= args.warmup:
+            vals.append((gbs, sec))
+    value = statistics.median(v for v, _ in vals)
+    ms = statistics.median(s for _, s in vals) * 1e3
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "config2 (bounded CPU sample)", "sample": desc},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": thr, "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py (ours) needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    try:
+        res = run_ours(args, rank, world, dev)
+        if rank == 0:
+            if not args.no_cpu_baseline and world == 1:
+                gbs, sec, thr, desc = cpu_reference_sample(8192)
+                res["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
+                                       "sample": desc + f"; {sec * 1e3:.1f} ms per pass"}
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,260 @@
+/*
+ * specverify.h -- C ABI of the B200 (sm_100a) tree-verification library.
+ *
+ * One shared library (libspecverify.so) holds every kernel of DiffSpec's
+ * target-side tree-verification hot path.  All entry points:
+ *   - are extern "C", take plain device pointers, element strides and sizes,
+ *     and a cudaStream_t (passed as void*; NULL = legacy default stream);
+ *   - never allocate or free device memory: the caller passes outputs and any
+ *     workspace (sized by the *_workspace_size queries);
+ *   - are stream-ordered and never synchronise the host;
+ *   - return TV_OK (0) or a negative tv_status; they never trap on the GPU.
+ *     Argument errors are detected on the host before any launch; errors the
+ *     kernels detect (bad parent pointers, page ids out of range) are written
+ *     to a status word in device memory that the caller reads back.
+ *
+ * Element strides are in elements of the tensor's own dtype; the innermost
+ * (head_dim) stride must be 1.  Byte strides are named *_bytes.
+ *
+ * Reference interfaces replaced (paths inside the reference package
+ * ``diffspec``):
+ *   tv_verify_attn        diffspec/runtime/tree_attention.py:414-446
+ *                         (prefix_attention_forward), :462-539
+ *                         (tree_attention_forward), and the merge at
+ *                         diffspec/runtime/llama_target_model.py:835-864;
+ *                         diffspec/runtime/bundle_verifier.py:166-257
+ *                         (FusedBundleVerifier.verify_bundle) and :341-366
+ *                         (PagedBundleVerifier.verify_bundle_paged)
+ *   tv_merge_partials     diffspec/runtime/tree_attention.py:535-539 (LSE merge)
+ *   tv_pack_mask          diffspec/runtime/tree_attention.py:449-460
+ *   tv_accept             diffspec/draft/tree_verification.py:100-182
+ *   tv_compact_contig     diffspec/draft/tree_verification.py:197-217,
+ *                         diffspec/runtime/cache_state.py:38-50
+ *   tv_copy_pages,
+ *   tv_compact_paged      diffspec/core/kv_cache/paged_kv.py:168-223 (COW)
+ *   tv_arena_gather       diffspec/core/kv_cache/chunk_arena.py:126-173
+ *   tv_gather_page_table  diffspec/core/kv_cache/chunk_arena.py:86-178 (zero-copy form)
+ */
+#ifndef SPECVERIFY_H_
+#define SPECVERIFY_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------- */
+enum tv_status {
+  TV_OK = 0,
+  TV_ERR_SHAPE = -1,       /* inconsistent or unsupported sizes           */
+  TV_ERR_DTYPE = -2,       /* unsupported element type                    */
+  TV_ERR_ALIGN = -3,       /* pointer / stride not 16-byte aligned        */
+  TV_ERR_LAUNCH = -4,      /* CUDA launch or runtime error                */
+  TV_ERR_WORKSPACE = -5,   /* workspace missing or too small              */
+  TV_ERR_INPUT = -6,       /* invalid input values (device-detected)      */
+  TV_ERR_UNSUPPORTED = -7, /* valid request this build does not handle    */
+  TV_ERR_NULL = -8         /* required pointer is NULL                    */
+};
+
+enum tv_dtype { TV_BF16 = 0, TV_F16 = 1, TV_F32 = 2 };
+
+/* Human-readable text for a status code (static storage). */
+const char* tv_status_string(int status);
+/* Library version, e.g. "specverify 0.1 sm_100a". */
+const char* tv_version(void);
+/* Text of the last CUDA error an entry point saw on this host thread. */
+const char* tv_last_cuda_error(void);
+
+/* ---- verify attention ------------------------------------------------
+ *
+ * For every batch b, query row m (tree node) and query head h (KV head
+ * h / (heads / kv_heads)):
+ *
+ *   out[b,m,h,:] = softmax_n(scale * q[b,m,h,:] . k[b,n,hk,:]) @ v[b,n,hk,:]
+ *   lse[b,m,h]   = log sum_n exp(scale * q . k)        (natural log)
+ *
+ * over the keys n < len_b visible to row m: every key before
+ * tail_b = len_b - mask_len, and key tail_b + j when bit j of the row's mask
+ * is set (word j / 64, bit j % 64 of mask[b * mask_sb + m * mask_sm + ...]).
+ * len_b = kv_lens[b] if kv_lens != NULL, else num_keys.
+ * A row with no visible key gets out = 0 and lse = -inf.
+ *
+ * KV addressing:
+ *   contiguous (page_table == NULL): key n of (b, hk) starts at
+ *       k + b * k_sb + n * k_sn + hk * k_sh;
+ *   paged: page = page_table[b * pt_sb + n / page_size]; the key starts at
+ *       k + page * k_sb + hk * k_sh + (n % page_size) * k_sn
+ *     (k_sb is the page stride); a negative page id reads as zeros.
+ * v uses its own v_* strides the same way.
+ *
+ * Optional epilogues: lse (fp32, strided) and, when aux_lse != NULL,
+ *   weight[b,m,h] = (dtype) sigmoid(aux_lse[b,m,h] - lse[b,m,h])
+ * (the merge weight of tree_attention.py:539).
+ * out_f32 != 0 writes out in fp32 instead of `dtype`.
+ *
+ * Work is split over the keys (split-KV); the partial (O, lse) pairs live in
+ * the caller's workspace and are merged by log-sum-exp in a second kernel.
+ */
+typedef struct tv_attn_args {
+  int32_t dtype;                 /* TV_BF16 or TV_F16 for q, k, v, out      */
+  int32_t batch, rows, heads, kv_heads, head_dim;
+  float scale;                   /* softmax scale, usually 1/sqrt(head_dim) */
+  const void* q;
+  int64_t q_sb, q_sm, q_sh;
+  const void* k;
+  const void* v;
+  int64_t k_sb, k_sn, k_sh;
+  int64_t v_sb, v_sn, v_sh;
+  const int32_t* page_table;     /* NULL = contiguous KV                    */
+  int64_t pt_sb;
+  int32_t page_size;
+  int32_t num_pages;             /* physical pages in the pool (bounds check)*/
+  const int32_t* kv_lens;        /* optional per-batch key counts (device)  */
+  int32_t num_keys;
+  int32_t mask_len;              /* keys gated by the bitmask (0 = none)    */
+  const uint64_t* mask;
+  int64_t mask_sb, mask_sm;
+  void* out;
+  int64_t o_sb, o_sm, o_sh;
+  int32_t out_f32;
+  float* lse;                    /* optional                                */
+  int64_t lse_sb, lse_sm, lse_sh;
+  const float* aux_lse;          /* optional: prefix LSE for the weight     */
+  int64_t aux_sb, aux_sm, aux_sh;
+  void* weight;                  /* required when aux_lse != NULL           */
+  int64_t w_sb, w_sm, w_sh;
+  int32_t num_splits;            /* 0 = choose automatically                */
+  int32_t kernel;                /* 0 = auto, 1 = mma.sync path, 2 = tcgen05*/
+  void* workspace;
+  size_t workspace_bytes;
+} tv_attn_args;
+
+int tv_attn_workspace_size(const tv_attn_args* args, size_t* bytes);
+int tv_verify_attn(const tv_attn_args* args, void* stream);
+
+/* Merge `parts` partial attentions over disjoint key sets (split-KV or one
+ * per rank of a sequence-sharded cache):
+ *   parts_o   [parts][rows][head_dim] fp32, each normalised over its keys
+ *   parts_lse [parts][rows] fp32 natural-log LSE
+ * writes out [rows][head_dim] (out_dtype) and, if out_lse != NULL, the merged
+ * LSE [rows].  Part p of row r is parts_o + p * part_stride + r * head_dim. */
+int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
+                      const float* parts_o, int64_t part_stride_o,
+                      const float* parts_lse, int64_t part_stride_lse,
+                      int32_t out_dtype, void* out, float* out_lse, void* stream);
+
+/* ---- masks --------------------------------------------------------------
+ * Pack a [batch][rows][cols] keep-mask into bits: bit c of row r is set when
+ *   kind 0 (int8/uint8/bool): element != 0
+ *   kind 1 (fp32), 2 (fp16), 3 (bf16): element == 0   (additive float mask)
+ * Element (b, r, c) is at src + b*s_b + r*s_r + c*s_c (elements).
+ * out: [batch][rows][words] uint64, words = out_sr >= ceil(cols/64),
+ * row stride out_sr words, batch stride out_sb words. */
+int tv_pack_mask(int32_t kind, const void* src, int64_t s_b, int64_t s_r, int64_t s_c,
+                 int32_t batch, int32_t rows, int32_t cols,
+                 uint64_t* out, int64_t out_sb, int64_t out_sr, void* stream);
+
+/* ---- acceptance --------------------------------------------------------
+ * One target token per node, then the acceptance rule of verify_new:
+ *   ok[i] = draft[i] == next[parent(i)], ok[0] = 1, closure
+ *   ok &= ok[parent] for min(max_depth + 2, rows) synchronous rounds,
+ *   best = first argmax of (ok ? pos : 0), path = root .. best.
+ * mode 0: next = argmax over the vocabulary (first maximum; NaN counts as
+ *         the maximum, first NaN wins);
+ * mode 1: next = sample from softmax(logits / temperature) by the Gumbel-max
+ *         rule with counter-based Philox4x32-10 noise keyed by (seed, offset,
+ *         row, token);
+ * mode 2: next = sampled[] given by the caller.
+ * parent[] has rows-1 entries: the parent's index among draft nodes, -1 for
+ * children of the root (a value equal to its own index also means -1).
+ *
+ * result (device int64, length 8 + 2*rows):
+ *   [0] status (0 ok, else TV_ERR_INPUT: parent out of range / cycle)
+ *   [1] best (max_id)    [2] path length n = accept_length + 1
+ *   [3] next_token       [4..7] reserved
+ *   [8 .. 8+rows)        path node ids, root first
+ *   [8+rows .. 8+2rows)  path draft tokens
+ * next_tokens (device int64 [rows]) receives the per-node target tokens.
+ * workspace: tv_accept_workspace_size() bytes. */
+typedef struct tv_accept_args {
+  int32_t mode;
+  int32_t logits_dtype;          /* TV_BF16, TV_F16 or TV_F32               */
+  const void* logits;
+  int64_t logits_sm;             /* row stride (elements)                   */
+  int32_t rows, vocab;
+  const int64_t* draft;          /* [rows]                                  */
+  const int64_t* parent;         /* [rows - 1]                              */
+  const int64_t* pos;            /* [rows]                                  */
+  int32_t max_depth;
+  const int64_t* sampled;        /* mode 2                                  */
+  float temperature;             /* mode 1                                  */
+  uint64_t seed, offset;         /* mode 1                                  */
+  int64_t* next_tokens;
+  int64_t* result;
+  void* workspace;
+  size_t workspace_bytes;
+} tv_accept_args;
+
+int tv_accept_workspace_size(const tv_accept_args* args, size_t* bytes);
+int tv_accept(const tv_accept_args* args, void* stream);
+
+/* ---- compaction -------------------------------------------------------
+ * Contiguous cache: for every slice s < num_slices of `data`
+ * (slice base = data + s * slice_stride_bytes, row r at
+ * + r * row_stride_bytes, row_bytes bytes per row) move row
+ * start + path[j] to start + j for j < n, gathering all rows of a slice
+ * before writing any.  path and n are read from an accept result buffer on
+ * the device (n <= max_rows). */
+int tv_compact_contig(void* data, int64_t num_slices, int64_t slice_stride_bytes,
+                      int64_t row_stride_bytes, int32_t row_bytes, int64_t start,
+                      const int64_t* accept_result, int32_t max_rows, void* stream);
+
+/* Paged pool copy-on-write: copy whole pages src -> dst for every plane
+ * (plane = layer x K/V) and head.  pairs: device int32 [npairs][2] (src, dst).
+ * Page p of plane l starts at pool + l * plane_stride_bytes
+ * + p * page_stride_bytes; page_bytes contiguous bytes per page. */
+int tv_copy_pages(void* pool, int32_t planes, int64_t plane_stride_bytes,
+                  int64_t page_stride_bytes, int64_t page_bytes,
+                  const int32_t* pairs, int32_t npairs, int32_t num_pages, void* stream);
+
+/* Paged compaction: move logical row start + path[j] to start + j for every
+ * plane and head.  Sources are read through `src_table` (logical page ->
+ * physical page before the move), destinations written through `dst_table`
+ * (after the caller's copy-on-write remap; run tv_copy_pages first).  Both
+ * are device int32 [table_len].  Row (plane l, page p, head h, offset o)
+ * starts at pool + l*plane_stride_bytes + p*page_stride_bytes
+ * + h*head_stride_bytes + o*row_stride_bytes.  A negative page id reads as
+ * zeros and is never written. */
+int tv_compact_paged(void* pool, int32_t planes, int32_t heads, int64_t plane_stride_bytes,
+                     int64_t page_stride_bytes, int64_t head_stride_bytes,
+                     int64_t row_stride_bytes, int32_t row_bytes, int32_t page_size,
+                     const int32_t* src_table, const int32_t* dst_table, int32_t table_len,
+                     int32_t num_pages, int64_t start, const int64_t* accept_result,
+                     int32_t max_rows, void* stream);
+
+/* Chunk arena gather: for every copy (chunk c, arena slot o), layer l, K/V
+ * and head h, copy rows [c*chunk, min((c+1)*chunk, src_len)) of the source
+ * layer cache into arena rows [o*chunk, ...).
+ *   src_k / src_v: device uint64 [layers] base pointers of [heads][src_len] rows
+ *   (head stride src_head_stride_bytes, row stride src_row_stride_bytes);
+ *   arena row (l, kv, h, r) at arena + l*arena_layer_stride_bytes
+ *   + kv*arena_kv_stride_bytes + h*arena_head_stride_bytes + r*row_bytes.
+ * copies: device int32 [ncopies][2]. */
+int tv_arena_gather(int32_t layers, int32_t heads, const uint64_t* src_k, const uint64_t* src_v,
+                    int64_t src_head_stride_bytes, int64_t src_row_stride_bytes, int32_t src_len,
+                    void* arena, int64_t arena_layer_stride_bytes, int64_t arena_kv_stride_bytes,
+                    int64_t arena_head_stride_bytes, int32_t row_bytes, int32_t chunk_size,
+                    int32_t arena_rows, const int32_t* copies, int32_t ncopies, void* stream);
+
+/* Zero-copy arena: out[i * pages_per_chunk + j] =
+ *   page_table[chunk_ids[i] * pages_per_chunk + j] for i < nchunks. */
+int tv_gather_page_table(const int32_t* page_table, int32_t table_len, const int32_t* chunk_ids,
+                         int32_t nchunks, int32_t pages_per_chunk, int32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECVERIFY_H_ */

@@ -1,0 +1,316 @@
+// C ABI of verify attention: argument checks, split-KV planning, kernel
+// selection, and the log-sum-exp merge kernels.
+#include <string.h>
+
+#include <string>
+
+#include "attn_epilogue.cuh"
+#include "attn_kernels.cuh"
+
+namespace tv {
+
+static thread_local std::string g_last_cuda_error;
+
+int record_cuda_error(cudaError_t e) {
+  g_last_cuda_error = cudaGetErrorString(e);
+  return TV_ERR_LAUNCH;
+}
+
+namespace {
+
+// ---- split combine: one warp per query row ----------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) {
+  constexpr int PER = D / 32;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+  const int64_t total = (int64_t)p.B * p.Hkv * p.R;
+  if (row >= total) return;
+  const int bh = (int)(row / p.R);
+  const int r = (int)(row - (int64_t)bh * p.R);
+  const int b = bh / p.Hkv;
+  const int hk = bh - b * p.Hkv;
+
+  float mx = -INFINITY;
+  for (int s = lane; s < p.splits; s += 32) mx = fmaxf(mx, *part_lse_row(p, s, bh, r));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+  float wsum = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < p.splits; ++s) {
+      const float l = *part_lse_row(p, s, bh, r);
+      if (l == -INFINITY) continue;
+      const float w = expf(l - mx);
+      wsum += w;
+      const float* src = part_o_row(p, s, bh, r, D) + lane * PER;
+#pragma unroll
+      for (int i = 0; i < PER; i += 2) {
+        const float2 v = *reinterpret_cast<const float2*>(src + i);
+        acc[i] += w * v.x;
+        acc[i + 1] += w * v.y;
+      }
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const float lse = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+  int m, h;
+  row_coords(p, hk, r, m, h);
+#pragma unroll
+  for (int i = 0; i < PER; i += 2) store_out_pair<T>(p, b, m, h, lane * PER + i, acc[i] * inv, acc[i + 1] * inv);
+  if (lane == 0) store_row_stats<T>(p, b, m, h, lse);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_plain(void* out, int64_t off, float v) {
+  static_cast<T*>(out)[off] = Elem<T>::from_f(v);
+}
+template <>
+__device__ __forceinline__ void store_plain<float>(void* out, int64_t off, float v) {
+  static_cast<float*>(out)[off] = v;
+}
+
+// ---- generic merge of `parts` partials (split-KV or one per rank) -------------
+template <typename OutT>
+__global__ void __launch_bounds__(128) merge_parts_kernel(int parts, int64_t rows, int D, const float* po,
+                                                          int64_t pso, const float* pl, int64_t psl, void* out,
+                                                          float* out_lse) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+  if (row >= rows) return;
+  float mx = -INFINITY;
+  for (int s = lane; s < parts; s += 32) mx = fmaxf(mx, pl[s * psl + row]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float wsum = 0.f;
+  for (int s = 0; s < parts && mx != -INFINITY; ++s) {
+    const float l = pl[s * psl + row];
+    if (l != -INFINITY) wsum += expf(l - mx);
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  for (int d = lane; d < D; d += 32) {
+    float acc = 0.f;
+    for (int s = 0; s < parts && mx != -INFINITY; ++s) {
+      const float l = pl[s * psl + row];
+      if (l == -INFINITY) continue;
+      acc += expf(l - mx) * po[s * pso + row * D + d];
+    }
+    store_plain<OutT>(out, row * D + d, acc * inv);
+  }
+  if (lane == 0 && out_lse) out_lse[row] = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+}
+
+bool stride_ok(int64_t s) { return (s % 8) == 0; }
+
+int validate(const tv_attn_args* a) {
+  if (!a) return TV_ERR_NULL;
+  if (a->dtype != TV_BF16 && a->dtype != TV_F16) return TV_ERR_DTYPE;
+  if (a->batch < 0 || a->rows < 0 || a->heads <= 0 || a->kv_heads <= 0) return TV_ERR_SHAPE;
+  if (a->heads % a->kv_heads != 0) return TV_ERR_SHAPE;
+  if (a->head_dim != 64 && a->head_dim != 128) return TV_ERR_UNSUPPORTED;
+  if (a->num_keys < 0 || a->mask_len < 0) return TV_ERR_SHAPE;
+  if (a->batch == 0 || a->rows == 0) return TV_OK;
+  if (!a->q || !a->out) return TV_ERR_NULL;
+  if (a->num_keys > 0 && (!a->k || !a->v)) return TV_ERR_NULL;
+  if (a->mask_len > 0 && !a->mask) return TV_ERR_NULL;
+  if (!a->kv_lens && a->mask_len > a->num_keys) return TV_ERR_SHAPE;
+  if (a->aux_lse && !a->weight) return TV_ERR_NULL;
+  if (!aligned16(a->q) || !stride_ok(a->q_sb) || !stride_ok(a->q_sm) || !stride_ok(a->q_sh)) return TV_ERR_ALIGN;
+  if (a->num_keys > 0) {
+    if (!aligned16(a->k) || !aligned16(a->v)) return TV_ERR_ALIGN;
+    if (!stride_ok(a->k_sb) || !stride_ok(a->k_sn) || !stride_ok(a->k_sh)) return TV_ERR_ALIGN;
+    if (!stride_ok(a->v_sb) || !stride_ok(a->v_sn) || !stride_ok(a->v_sh)) return TV_ERR_ALIGN;
+  }
+  // Output rows are written two elements at a time.
+  const size_t esz = a->out_f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(a->out) % (2 * esz)) != 0) return TV_ERR_ALIGN;
+  if ((a->o_sb | a->o_sm | a->o_sh) & 1) return TV_ERR_ALIGN;
+  if (a->page_table) {
+    if (a->page_size <= 0 || (a->page_size & (a->page_size - 1))) return TV_ERR_UNSUPPORTED;
+    if (a->num_pages <= 0) return TV_ERR_SHAPE;
+  }
+  return TV_OK;
+}
+
+struct Plan {
+  bool tc;
+  int tile;
+  int splits;
+  int tiles_per_split;
+};
+
+Plan plan(const tv_attn_args* a) {
+  const int D = a->head_dim;
+  const int G = a->heads / a->kv_heads;
+  const int R = a->rows * G;
+  const bool paged = a->page_table != nullptr;
+  int shift = 0;
+  if (paged) while ((1 << shift) < a->page_size) ++shift;
+  Plan pl;
+  pl.tc = (a->kernel != 1) && tc_supported(a->dtype, D, R, paged, shift);
+  if (a->kernel == 2 && !pl.tc) pl.tc = false;
+  pl.tile = pl.tc ? tc_tile_keys() : mma_tile_keys();
+  const int rows_per_cta = pl.tc ? tc_rows_per_cta() : mma_rows_per_cta();
+  const int row_blocks = (R + rows_per_cta - 1) / rows_per_cta;
+  const int64_t base = (int64_t)row_blocks * a->batch * a->kv_heads;
+  const int tiles = (a->num_keys + pl.tile - 1) / pl.tile;
+  int splits = a->num_splits;
+  if (splits <= 0) {
+    // Aim for two waves of CTAs over the 148 SMs (more for the small-CTA path).
+    const int64_t target = pl.tc ? kNumSMs : 4LL * kNumSMs;
+    splits = (int)((target + base - 1) / base);
+  }
+  if (splits > tiles) splits = tiles;
+  if (splits > 256) splits = 256;
+  if (splits < 1) splits = 1;
+  pl.tiles_per_split = tiles > 0 ? (tiles + splits - 1) / splits : 1;
+  pl.splits = tiles > 0 ? (tiles + pl.tiles_per_split - 1) / pl.tiles_per_split : 1;
+  return pl;
+}
+
+size_t workspace_for(const tv_attn_args* a, const Plan& pl) {
+  if (pl.splits <= 1) return 0;
+  const int G = a->heads / a->kv_heads;
+  const int64_t rows = (int64_t)a->batch * a->kv_heads * a->rows * G;
+  const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);
+  const size_t l = (size_t)pl.splits * rows * sizeof(float);
+  return ((o + 255) & ~size_t(255)) + l;
+}
+
+}  // namespace
+
+int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st) {
+  const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
+  dim3 grid((unsigned)((rows + 3) / 4));
+  if (dtype == TV_BF16) {
+    if (D == 128) split_combine_kernel<__nv_bfloat16, 128><<<grid, 128, 0, st>>>(p);
+    else split_combine_kernel<__nv_bfloat16, 64><<<grid, 128, 0, st>>>(p);
+  } else {
+    if (D == 128) split_combine_kernel<__half, 128><<<grid, 128, 0, st>>>(p);
+    else split_combine_kernel<__half, 64><<<grid, 128, 0, st>>>(p);
+  }
+  return check_launch();
+}
+
+}  // namespace tv
+
+using namespace tv;
+
+extern "C" {
+
+const char* tv_status_string(int s) {
+  switch (s) {
+    case TV_OK: return "ok";
+    case TV_ERR_SHAPE: return "inconsistent or unsupported sizes";
+    case TV_ERR_DTYPE: return "unsupported element type";
+    case TV_ERR_ALIGN: return "pointer or stride not 16-byte aligned";
+    case TV_ERR_LAUNCH: return "CUDA launch or runtime error";
+    case TV_ERR_WORKSPACE: return "workspace missing or too small";
+    case TV_ERR_INPUT: return "invalid input values";
+    case TV_ERR_UNSUPPORTED: return "request not supported by this build";
+    case TV_ERR_NULL: return "required pointer is NULL";
+    default: return "unknown status";
+  }
+}
+
+const char* tv_version(void) { return "specverify 0.1 sm_100a"; }
+
+const char* tv_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
+
+int tv_attn_workspace_size(const tv_attn_args* a, size_t* bytes) {
+  if (!bytes) return TV_ERR_NULL;
+  *bytes = 0;
+  const int v = validate(a);
+  if (v != TV_OK) return v;
+  if (a->batch == 0 || a->rows == 0) return TV_OK;
+  *bytes = workspace_for(a, plan(a));
+  return TV_OK;
+}
+
+int tv_verify_attn(const tv_attn_args* a, void* stream) {
+  const int v = validate(a);
+  if (v != TV_OK) return v;
+  if (a->batch == 0 || a->rows == 0) return TV_OK;
+  const Plan pl = plan(a);
+  const size_t need = workspace_for(a, pl);
+  if (need > 0 && (!a->workspace || a->workspace_bytes < need)) return TV_ERR_WORKSPACE;
+  if (need > 0 && !aligned16(a->workspace)) return TV_ERR_ALIGN;
+
+  AttnParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = a->q;
+  p.q_sb = a->q_sb; p.q_sm = a->q_sm; p.q_sh = a->q_sh;
+  p.k = a->k ? a->k : a->q;
+  p.v = a->v ? a->v : a->q;
+  p.k_sb = a->k_sb; p.k_sn = a->k_sn; p.k_sh = a->k_sh;
+  p.v_sb = a->v_sb; p.v_sn = a->v_sn; p.v_sh = a->v_sh;
+  p.pt = a->page_table;
+  p.pt_sb = a->pt_sb;
+  p.page_shift = 0;
+  if (a->page_table) while ((1 << p.page_shift) < a->page_size) ++p.page_shift;
+  p.num_pages = a->num_pages;
+  p.kv_lens = a->kv_lens;
+  p.num_keys = a->num_keys;
+  p.mask_len = a->mask_len;
+  p.mask = a->mask;
+  p.mask_sb = a->mask_sb; p.mask_sm = a->mask_sm;
+  p.B = a->batch; p.M = a->rows; p.H = a->heads; p.Hkv = a->kv_heads;
+  p.G = a->heads / a->kv_heads;
+  p.R = a->rows * p.G;
+  p.scale_log2 = a->scale * kLog2e;
+  p.splits = pl.splits;
+  p.tiles_per_split = pl.tiles_per_split;
+  p.out = a->out;
+  p.o_sb = a->o_sb; p.o_sm = a->o_sm; p.o_sh = a->o_sh;
+  p.out_f32 = a->out_f32;
+  p.lse = a->lse;
+  p.lse_sb = a->lse_sb; p.lse_sm = a->lse_sm; p.lse_sh = a->lse_sh;
+  p.aux = a->aux_lse;
+  p.aux_sb = a->aux_sb; p.aux_sm = a->aux_sm; p.aux_sh = a->aux_sh;
+  p.weight = a->weight;
+  p.w_sb = a->w_sb; p.w_sm = a->w_sm; p.w_sh = a->w_sh;
+  if (pl.splits > 1) {
+    const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
+    const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);
+    p.part_o = static_cast<float*>(a->workspace);
+    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + ((o + 255) & ~size_t(255)));
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = pl.tc ? launch_attn_tc(p, a->dtype, a->head_dim, st) : launch_attn_mma(p, a->dtype, a->head_dim, st);
+  if (rc != TV_OK) return rc;
+  if (pl.splits > 1) rc = launch_split_combine(p, a->dtype, a->head_dim, st);
+  return rc;
+}
+
+int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim, const float* parts_o, int64_t part_stride_o,
+                      const float* parts_lse, int64_t part_stride_lse, int32_t out_dtype, void* out, float* out_lse,
+                      void* stream) {
+  if (parts <= 0 || rows < 0 || head_dim <= 0) return TV_ERR_SHAPE;
+  if (rows == 0) return TV_OK;
+  if (!parts_o || !parts_lse || !out) return TV_ERR_NULL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)((rows + 3) / 4));
+  switch (out_dtype) {
+    case TV_BF16:
+      merge_parts_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(parts, rows, head_dim, parts_o, part_stride_o,
+                                                              parts_lse, part_stride_lse, out, out_lse);
+      break;
+    case TV_F16:
+      merge_parts_kernel<__half><<<grid, 128, 0, st>>>(parts, rows, head_dim, parts_o, part_stride_o, parts_lse,
+                                                       part_stride_lse, out, out_lse);
+      break;
+    case TV_F32:
+      merge_parts_kernel<float><<<grid, 128, 0, st>>>(parts, rows, head_dim, parts_o, part_stride_o, parts_lse,
+                                                      part_stride_lse, out, out_lse);
+      break;
+    default: return TV_ERR_DTYPE;
+  }
+  return check_launch();
+}
+
+}  // extern "C"

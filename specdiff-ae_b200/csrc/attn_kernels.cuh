@@ -1,0 +1,24 @@
+// Host-side launchers of the verify-attention kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "attn_params.cuh"
+
+namespace tv {
+
+// Warp-MMA (mma.sync) path: any row count, head_dim 64 or 128.
+int launch_attn_mma(const AttnParams& p, int dtype, int D, cudaStream_t st);
+int mma_tile_keys();
+int mma_rows_per_cta();
+
+// Tensor-memory (tcgen05) path: head_dim 128, >= 64 query rows per KV head.
+int launch_attn_tc(const AttnParams& p, int dtype, int D, cudaStream_t st);
+bool tc_supported(int dtype, int D, int R, bool paged, int page_shift);
+int tc_tile_keys();
+int tc_rows_per_cta();
+
+// Log-sum-exp merge of split partials into the final outputs of AttnParams.
+int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st);
+
+}  // namespace tv

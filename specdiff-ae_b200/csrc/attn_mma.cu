@@ -1,0 +1,336 @@
+// Verify attention, warp-MMA path (mma.sync m16n8k16, fp32 accumulate).
+//
+// One CTA = 4 warps = 64 query rows of one (batch, KV head) over one split of
+// the keys.  Query rows are (tree node, query head of the GQA group) pairs,
+// r = node * G + g, so a KV tile staged in shared memory serves every head
+// of the group: nothing is expanded per query head (the reference
+// materialises repeat_kv copies, llama_target_model.py:795-796).
+//
+// Keys arrive in 64-key tiles by cp.async (16-byte chunks, zero-filled past
+// the end or for missing pages), double-buffered.  For a paged cache every key
+// looks up its physical page; the pool layout [page][kv_head][token][D] keeps
+// a page's 16 tokens of one head contiguous, so one 64-key tile is four 4 KB
+// runs.  Scores go through an online softmax in the exp2 domain; keys of the
+// tree tail are gated by one bit per (node, key) instead of the reference's
+// int8 [M, M] mask (tree_attention.py:449-460).
+//
+// This path serves narrow trees (fewer than 64 query rows per KV head) and
+// every shape the tensor-memory path does not take.
+#include "attn_epilogue.cuh"
+#include "attn_kernels.cuh"
+
+namespace tv {
+namespace {
+
+constexpr int BM = 64;      // query rows per CTA
+constexpr int BN = 64;      // keys per tile
+constexpr int NTHREADS = 128;
+constexpr int STAGES = 2;
+
+template <int D>
+struct Geo {
+  static constexpr int ROWB = D * 2;             // bytes per staged row
+  static constexpr int CH = ROWB / 16;           // 16-byte chunks per row
+  static constexpr int SW = CH < 8 ? CH : 8;     // swizzle period
+  static __device__ __forceinline__ int swz(int row, int c) { return row * ROWB + ((c ^ (row & (SW - 1))) << 4); }
+  static constexpr int Q_BYTES = BM * ROWB;
+  static constexpr int T_BYTES = BN * ROWB;
+  static constexpr int SMEM = Q_BYTES + 2 * STAGES * T_BYTES;
+};
+
+template <typename T, int D, bool PAGED>
+__device__ __forceinline__ void load_kv_tile(const AttnParams& p, uint8_t* sK, uint8_t* sV, int b, int hk, int len,
+                                             int tile, int tid) {
+  using G = Geo<D>;
+  const T* kb = static_cast<const T*>(p.k);
+  const T* vb = static_cast<const T*>(p.v);
+#pragma unroll
+  for (int j = 0; j < (BN * G::CH) / NTHREADS; ++j) {
+    const int idx = tid + j * NTHREADS;
+    const int row = idx / G::CH;
+    const int c = idx % G::CH;
+    const int n = tile * BN + row;
+    const T* ks = kb;
+    const T* vs = vb;
+    int bytes = 0;
+    if (n < len) {
+      if (PAGED) {
+        const int page = p.pt[(int64_t)b * p.pt_sb + (n >> p.page_shift)];
+        if (page >= 0 && page < p.num_pages) {
+          const int off = n & ((1 << p.page_shift) - 1);
+          ks = kb + (int64_t)page * p.k_sb + (int64_t)hk * p.k_sh + (int64_t)off * p.k_sn + c * 8;
+          vs = vb + (int64_t)page * p.v_sb + (int64_t)hk * p.v_sh + (int64_t)off * p.v_sn + c * 8;
+          bytes = 16;
+        }
+      } else {
+        ks = kb + (int64_t)b * p.k_sb + (int64_t)n * p.k_sn + (int64_t)hk * p.k_sh + c * 8;
+        vs = vb + (int64_t)b * p.v_sb + (int64_t)n * p.v_sn + (int64_t)hk * p.v_sh + c * 8;
+        bytes = 16;
+      }
+    }
+    cp_async16(smem_u32(sK + G::swz(row, c)), ks, bytes);
+    cp_async16(smem_u32(sV + G::swz(row, c)), vs, bytes);
+  }
+}
+
+template <typename T, int D, bool PAGED>
+__global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) {
+  using G = Geo<D>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + G::Q_BYTES;
+  uint8_t* sV = sK + STAGES * G::T_BYTES;
+
+  const int rb = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int split = blockIdx.z;
+  const int b = bh / p.Hkv;
+  const int hk = bh - b * p.Hkv;
+  int len = p.kv_lens ? p.kv_lens[b] : p.num_keys;
+  len = len < 0 ? 0 : len;
+  const int tail = len - p.mask_len;
+  const int ntiles = (len + BN - 1) / BN;
+  const int t0 = split * p.tiles_per_split;
+  const int t1 = min(ntiles, t0 + p.tiles_per_split);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+
+  // ---- stage the 64 query rows of this CTA --------------------------------
+  {
+    const T* qb = static_cast<const T*>(p.q);
+#pragma unroll
+    for (int j = 0; j < (BM * G::CH) / NTHREADS; ++j) {
+      const int idx = tid + j * NTHREADS;
+      const int row = idx / G::CH;
+      const int c = idx % G::CH;
+      const int r = rb * BM + row;
+      const T* src = qb;
+      int bytes = 0;
+      if (r < p.R) {
+        int m, h;
+        row_coords(p, hk, r, m, h);
+        src = qb + (int64_t)b * p.q_sb + (int64_t)m * p.q_sm + (int64_t)h * p.q_sh + c * 8;
+        bytes = 16;
+      }
+      cp_async16(smem_u32(sQ + G::swz(row, c)), src, bytes);
+    }
+  }
+  if (t0 < t1) load_kv_tile<T, D, PAGED>(p, sK, sV, b, hk, len, t0, tid);
+  cp_async_commit();
+
+  // Rows held by this thread: warp rows gid and gid + 8.
+  const int r0 = rb * BM + warp * 16 + gid;
+  const int r1 = r0 + 8;
+  const int m0 = min(r0, p.R - 1) / p.G;
+  const int m1 = min(r1, p.R - 1) / p.G;
+  const uint64_t* mrow0 = p.mask ? p.mask + (int64_t)b * p.mask_sb + (int64_t)m0 * p.mask_sm : nullptr;
+  const uint64_t* mrow1 = p.mask ? p.mask + (int64_t)b * p.mask_sb + (int64_t)m1 * p.mask_sm : nullptr;
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mx0 = -INFINITY, mx1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  uint32_t qf[D / 16][4];
+
+  for (int t = t0; t < t1; ++t) {
+    const int st = (t - t0) & 1;
+    if (t + 1 < t1) {
+      load_kv_tile<T, D, PAGED>(p, sK + (st ^ 1) * G::T_BYTES, sV + (st ^ 1) * G::T_BYTES, b, hk, len, t + 1, tid);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (t == t0) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kk * 2 + (lane >> 4);
+        ldsm_x4(smem_u32(sQ + G::swz(row, c)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      }
+    }
+    const uint8_t* tK = sK + st * G::T_BYTES;
+    const uint8_t* tV = sV + st * G::T_BYTES;
+
+    // ---- S = Q K^T (16 rows x 64 keys per warp) ---------------------------
+    float s[BN / 8][4];
+#pragma unroll
+    for (int i = 0; i < BN / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int nn = 0; nn < BN / 16; ++nn) {
+        const int row = nn * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(tK + G::swz(row, c)), b0, b1, b2, b3);
+        Mma<T>::run(s[2 * nn], qf[kk], b0, b1);
+        Mma<T>::run(s[2 * nn + 1], qf[kk], b2, b3);
+      }
+    }
+
+    // ---- scale, bound and tree-mask the scores -----------------------------
+    const int nbase = t * BN;
+    const bool edge = (nbase + BN > len) || (nbase + BN > tail);
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x = s[j][e] * p.scale_log2;
+        if (edge) {
+          const int n = nbase + j * 8 + 2 * tig + (e & 1);
+          if (n >= len) {
+            x = -INFINITY;
+          } else if (n >= tail) {
+            const int rel = n - tail;
+            const uint64_t* mr = (e < 2) ? mrow0 : mrow1;
+            const uint64_t w = __ldg(mr + (rel >> 6));
+            if (!((w >> (rel & 63)) & 1ull)) x = -INFINITY;
+          }
+        }
+        s[j][e] = x;
+      }
+    }
+
+    // ---- online softmax (exp2 domain) --------------------------------------
+    float tmax0 = -INFINITY, tmax1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) {
+      tmax0 = fmaxf(tmax0, fmaxf(s[j][0], s[j][1]));
+      tmax1 = fmaxf(tmax1, fmaxf(s[j][2], s[j][3]));
+    }
+    tmax0 = fmaxf(tmax0, __shfl_xor_sync(0xffffffffu, tmax0, 1));
+    tmax0 = fmaxf(tmax0, __shfl_xor_sync(0xffffffffu, tmax0, 2));
+    tmax1 = fmaxf(tmax1, __shfl_xor_sync(0xffffffffu, tmax1, 1));
+    tmax1 = fmaxf(tmax1, __shfl_xor_sync(0xffffffffu, tmax1, 2));
+    const float nm0 = fmaxf(mx0, tmax0);
+    const float nm1 = fmaxf(mx1, tmax1);
+    const float use0 = nm0 == -INFINITY ? 0.f : nm0;
+    const float use1 = nm1 == -INFINITY ? 0.f : nm1;
+    const float a0 = fast_exp2(mx0 - use0);
+    const float a1 = fast_exp2(mx1 - use1);
+    mx0 = nm0;
+    mx1 = nm1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) {
+      s[j][0] = fast_exp2(s[j][0] - use0);
+      s[j][1] = fast_exp2(s[j][1] - use0);
+      s[j][2] = fast_exp2(s[j][2] - use1);
+      s[j][3] = fast_exp2(s[j][3] - use1);
+      ps0 += s[j][0] + s[j][1];
+      ps1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * a0 + ps0;
+    l1 = l1 * a1 + ps1;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= a0;
+      o[i][1] *= a0;
+      o[i][2] *= a1;
+      o[i][3] *= a1;
+    }
+
+    // ---- O += P V ------------------------------------------------------------
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk) {
+      uint32_t a[4];
+      a[0] = Elem<T>::pack2(s[2 * kk][0], s[2 * kk][1]);
+      a[1] = Elem<T>::pack2(s[2 * kk][2], s[2 * kk][3]);
+      a[2] = Elem<T>::pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      a[3] = Elem<T>::pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dd = 0; dd < D / 16; ++dd) {
+        const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = dd * 2 + (lane >> 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(tV + G::swz(row, c)), b0, b1, b2, b3);
+        Mma<T>::run(o[2 * dd], a, b0, b1);
+        Mma<T>::run(o[2 * dd + 1], a, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // ---- finish the rows -------------------------------------------------------
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+  const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const float lse0 = l0 > 0.f ? (mx0 + __log2f(l0)) * kLn2 : -INFINITY;
+  const float lse1 = l1 > 0.f ? (mx1 + __log2f(l1)) * kLn2 : -INFINITY;
+
+  if (p.splits == 1) {
+    if (r0 < p.R) {
+      int m, h;
+      row_coords(p, hk, r0, m, h);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) store_out_pair<T>(p, b, m, h, i * 8 + 2 * tig, o[i][0] * inv0, o[i][1] * inv0);
+      if (tig == 0) store_row_stats<T>(p, b, m, h, lse0);
+    }
+    if (r1 < p.R) {
+      int m, h;
+      row_coords(p, hk, r1, m, h);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) store_out_pair<T>(p, b, m, h, i * 8 + 2 * tig, o[i][2] * inv1, o[i][3] * inv1);
+      if (tig == 0) store_row_stats<T>(p, b, m, h, lse1);
+    }
+  } else {
+    if (r0 < p.R) {
+      float* dst = part_o_row(p, split, bh, r0, D);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i)
+        *reinterpret_cast<float2*>(dst + i * 8 + 2 * tig) = make_float2(o[i][0] * inv0, o[i][1] * inv0);
+      if (tig == 0) *part_lse_row(p, split, bh, r0) = lse0;
+    }
+    if (r1 < p.R) {
+      float* dst = part_o_row(p, split, bh, r1, D);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i)
+        *reinterpret_cast<float2*>(dst + i * 8 + 2 * tig) = make_float2(o[i][2] * inv1, o[i][3] * inv1);
+      if (tig == 0) *part_lse_row(p, split, bh, r1) = lse1;
+    }
+  }
+}
+
+template <typename T, int D, bool PAGED>
+int launch_t(const AttnParams& p, cudaStream_t st) {
+  constexpr int smem = Geo<D>::SMEM;
+  auto kern = attn_mma_kernel<T, D, PAGED>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  dim3 grid((p.R + BM - 1) / BM, p.B * p.Hkv, p.splits);
+  kern<<<grid, NTHREADS, smem, st>>>(p);
+  return check_launch();
+}
+
+template <typename T>
+int launch_dtype(const AttnParams& p, int D, cudaStream_t st) {
+  const bool paged = p.pt != nullptr;
+  switch (D) {
+    case 64: return paged ? launch_t<T, 64, true>(p, st) : launch_t<T, 64, false>(p, st);
+    case 128: return paged ? launch_t<T, 128, true>(p, st) : launch_t<T, 128, false>(p, st);
+    default: return TV_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace
+
+int mma_tile_keys() { return BN; }
+int mma_rows_per_cta() { return BM; }
+
+int launch_attn_mma(const AttnParams& p, int dtype, int D, cudaStream_t st) {
+  if (dtype == TV_BF16) return launch_dtype<__nv_bfloat16>(p, D, st);
+  if (dtype == TV_F16) return launch_dtype<__half>(p, D, st);
+  return TV_ERR_DTYPE;
+}
+
+}  // namespace tv

@@ -1,0 +1,127 @@
+"""Sequence-sharded verify attention across the GPUs of one node.
+
+The reference attends the whole prefix on one device
+(``llama_target_model.py:839-845``) and has no distributed code.  For long
+contexts the prefix KV is split into contiguous, page-aligned shards, one per
+rank.  Each rank runs the verify-attention kernel over its shard -- the rank
+that owns the tree tail also applies the tree bitmask to the M tree keys --
+and writes its partial ``(O_r fp32 [B, M, H, D], lse_r [B, M, H])`` into one
+packed buffer.  ONE ``all_gather`` over NCCL (NVLink/NVSwitch) exchanges the
+packed partials, and every rank merges them locally with ``tv_merge_partials``:
+
+    O = sum_r e^{lse_r - L} O_r / sum_r e^{lse_r - L},   L = max_r lse_r
+
+The gather is order-fixed, so every rank gets bit-identical results (the
+next layer's replicated projections need that).  An all-reduce formulation
+would need a max-reduce first: two collectives.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .. import _lib
+from .tree_attention import attention, pack_tree_mask
+
+
+def shard_bounds(total: int, world: int, rank: int, align: int = 1) -> Tuple[int, int]:
+    """Contiguous shard ``[lo, hi)`` of ``total`` tokens for ``rank``.
+
+    Shards are multiples of ``align`` tokens (a page) except the last; all
+    ranks but the last get ``ceil(total / world)`` rounded up to ``align``.
+    """
+    per = -(-total // world)
+    per = -(-per // align) * align
+    lo = min(total, rank * per)
+    hi = min(total, lo + per)
+    return lo, hi
+
+
+class PackedPartial:
+    """One rank's partial in a flat fp32 buffer: ``[O (B*M*H*D) | lse (B*M*H)]``."""
+
+    def __init__(self, b, m, h, d, device, dtype=torch.float32):
+        self.shape = (b, m, h, d)
+        self.n_o = b * m * h * d
+        self.n_l = b * m * h
+        self.buf = torch.empty(self.n_o + self.n_l, dtype=dtype, device=device)
+
+    @property
+    def numel(self):
+        return self.n_o + self.n_l
+
+    def o(self, buf=None):
+        return (self.buf if buf is None else buf)[: self.n_o].view(*self.shape)
+
+    def lse(self, buf=None):
+        b, m, h, _ = self.shape
+        return (self.buf if buf is None else buf)[self.n_o:].view(b, m, h)
+
+
+def merge_packed(gathered: torch.Tensor, part: PackedPartial, world: int, out_dtype: torch.dtype,
+                 out: Optional[torch.Tensor] = None, out_lse: Optional[torch.Tensor] = None):
+    """``tv_merge_partials`` over ``world`` packed partials laid end to end."""
+    b, m, h, d = part.shape
+    dev = _lib.require_cuda(gathered)
+    if out is None:
+        out = torch.empty((b, m, h, d), dtype=out_dtype, device=dev)
+    stride = part.numel
+    st = _lib.load().tv_merge_partials(world, b * m * h, d, gathered.data_ptr(), stride,
+                                       gathered.data_ptr() + part.n_o * gathered.element_size(), stride,
+                                       _lib.dtype_code(out_dtype), out.data_ptr(),
+                                       _lib.ptr(out_lse), _lib.stream_ptr(dev))
+    _lib.check(st, "tv_merge_partials")
+    return out
+
+
+class SequenceShardedVerify:
+    """Verify attention over a prefix sharded across the ranks of ``group``.
+
+    ``partial_fn`` computes this rank's partial into a :class:`PackedPartial`
+    (default: the CUDA kernel); ``merge_fn`` merges the gathered buffer
+    (default: ``tv_merge_partials``).  Both are replaceable so the host-side
+    exchange can be exercised with CPU ``gloo`` ranks.
+    """
+
+    def __init__(self, group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.partial_fn = partial_fn or self._cuda_partial
+        self.merge_fn = merge_fn or merge_packed
+        self._bufs = {}
+
+    def buffers(self, b, m, h, d, device):
+        key = (b, m, h, d, str(device))
+        if key not in self._bufs:
+            part = PackedPartial(b, m, h, d, device)
+            gathered = torch.empty(self.world * part.numel, dtype=part.buf.dtype, device=device)
+            self._bufs[key] = (part, gathered)
+        return self._bufs[key]
+
+    @staticmethod
+    def _cuda_partial(part: PackedPartial, q, k, v, num_keys, mask_bits, mask_len, page_table, num_splits):
+        attention(q, k, v, num_keys=num_keys, page_table=page_table, mask_bits=mask_bits, mask_len=mask_len,
+                  out=part.o(), lse=part.lse(), num_splits=num_splits)
+
+    def __call__(self, q, k_shard, v_shard, shard_len: int, tree_mask=None, *, page_table=None,
+                 out_dtype=None, num_splits: int = 0, return_lse: bool = False):
+        """q [B, M, H, D] (replicated); k_shard/v_shard: this rank's keys (contiguous
+        ``[B, n, Hkv, D]`` or a paged pool with ``page_table``), ``shard_len``
+        keys in all.  The rank holding the tree passes ``tree_mask`` (M x M keep
+        mask or packed bits) and has the M tree keys as its last ``M`` keys.
+        Returns the merged output on every rank."""
+        b, m, h, d = q.shape
+        part, gathered = self.buffers(b, m, h, d, q.device)
+        bits, mlen = None, 0
+        if tree_mask is not None:
+            bits = tree_mask if tree_mask.dtype == torch.int64 else pack_tree_mask(tree_mask, batch=b)
+            mlen = m
+        self.partial_fn(part, q, k_shard, v_shard, shard_len, bits, mlen, page_table, num_splits)
+        dist.all_gather_into_tensor(gathered, part.buf, group=self.group)
+        lse = torch.empty((b, m, h), dtype=torch.float32, device=q.device) if return_lse else None
+        out = self.merge_fn(gathered, part, self.world, out_dtype or q.dtype, out_lse=lse)
+        return (out, lse) if return_lse else out
