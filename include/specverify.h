@@ -126,9 +126,15 @@ typedef struct tv_attn_args {
   void* weight;                  /* required when aux_lse != NULL           */
   int64_t w_sb, w_sm, w_sh;
   int32_t num_splits;            /* 0 = choose automatically                */
-  int32_t kernel;                /* 0 = auto, 1 = mma.sync path, 2 = tcgen05*/
+  int32_t kernel;                /* bits 0-3: 0 auto, 1 warp-MMA, 2 tcgen05;
+                                    bit 4 (16): softmax weights as a hi+lo
+                                    16-bit pair in the PV product (automatic
+                                    for num_keys <= 4096)                   */
   void* workspace;
   size_t workspace_bytes;
+  int32_t* status;               /* optional device word, zeroed by the caller;
+                                    set nonzero if a kernel had to abandon a
+                                    wait (its output rows are then NaN)     */
 } tv_attn_args;
 
 int tv_attn_workspace_size(const tv_attn_args* args, size_t* bytes);

@@ -21,7 +21,8 @@ namespace {
 // ---- split combine: one warp per query row ----------------------------------
 template <typename T, int D>
 __global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) {
-  constexpr int PER = D / 32;
+  // Lane l owns head-dim pairs (2l, 2l+1), (2l+64, 2l+65), ...
+  constexpr int PER = D >= 64 ? D / 32 : 2;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 4 + warp;
@@ -47,12 +48,15 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) 
       if (l == -INFINITY) continue;
       const float w = expf(l - mx);
       wsum += w;
-      const float* src = part_o_row(p, s, bh, r, D) + lane * PER;
+      const float* src = part_o_row(p, s, bh, r, D);
 #pragma unroll
       for (int i = 0; i < PER; i += 2) {
-        const float2 v = *reinterpret_cast<const float2*>(src + i);
-        acc[i] += w * v.x;
-        acc[i + 1] += w * v.y;
+        const int d = 2 * lane + 32 * i;
+        if (d < D) {
+          const float2 v = *reinterpret_cast<const float2*>(src + d);
+          acc[i] += w * v.x;
+          acc[i + 1] += w * v.y;
+        }
       }
     }
   }
@@ -61,7 +65,10 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) 
   int m, h;
   row_coords(p, hk, r, m, h);
 #pragma unroll
-  for (int i = 0; i < PER; i += 2) store_out_pair<T>(p, b, m, h, lane * PER + i, acc[i] * inv, acc[i + 1] * inv);
+  for (int i = 0; i < PER; i += 2) {
+    const int d = 2 * lane + 32 * i;
+    if (d < D) store_out_pair<T>(p, b, m, h, d, acc[i] * inv, acc[i + 1] * inv);
+  }
   if (lane == 0) store_row_stats<T>(p, b, m, h, lse);
 }
 
@@ -107,12 +114,14 @@ __global__ void __launch_bounds__(128) merge_parts_kernel(int parts, int64_t row
 
 bool stride_ok(int64_t s) { return (s % 8) == 0; }
 
+constexpr int kPreciseMaxKeys = 4096;
+
 int validate(const tv_attn_args* a) {
   if (!a) return TV_ERR_NULL;
   if (a->dtype != TV_BF16 && a->dtype != TV_F16) return TV_ERR_DTYPE;
   if (a->batch < 0 || a->rows < 0 || a->heads <= 0 || a->kv_heads <= 0) return TV_ERR_SHAPE;
   if (a->heads % a->kv_heads != 0) return TV_ERR_SHAPE;
-  if (a->head_dim != 64 && a->head_dim != 128) return TV_ERR_UNSUPPORTED;
+  if (a->head_dim != 32 && a->head_dim != 64 && a->head_dim != 128) return TV_ERR_UNSUPPORTED;
   if (a->num_keys < 0 || a->mask_len < 0) return TV_ERR_SHAPE;
   if (a->batch == 0 || a->rows == 0) return TV_OK;
   if (!a->q || !a->out) return TV_ERR_NULL;
@@ -152,8 +161,13 @@ Plan plan(const tv_attn_args* a) {
   int shift = 0;
   if (paged) while ((1 << shift) < a->page_size) ++shift;
   Plan pl;
-  pl.tc = (a->kernel != 1) && tc_supported(a->dtype, D, R, paged, shift);
-  if (a->kernel == 2 && !pl.tc) pl.tc = false;
+  const int sel = a->kernel & 15;
+  // The tensor-memory kernel takes long, uniform-length key ranges whose last
+  // TMA box ends on a page / tile boundary (keys past the end are then whole
+  // out-of-range boxes, which TMA fills with zeros).
+  const int box = paged ? (a->page_size < 128 ? a->page_size : 128) : 1;
+  pl.tc = (sel != 1) && !(a->kernel & 16) && !a->kv_lens && a->num_keys > kPreciseMaxKeys &&
+          (a->num_keys % box) == 0 && tc_supported(a->dtype, D, R, paged, shift);
   pl.tile = pl.tc ? tc_tile_keys() : mma_tile_keys();
   const int rows_per_cta = pl.tc ? tc_rows_per_cta() : mma_rows_per_cta();
   const int row_blocks = (R + rows_per_cta - 1) / rows_per_cta;
@@ -161,9 +175,9 @@ Plan plan(const tv_attn_args* a) {
   const int tiles = (a->num_keys + pl.tile - 1) / pl.tile;
   int splits = a->num_splits;
   if (splits <= 0) {
-    // Aim for two waves of CTAs over the 148 SMs (more for the small-CTA path).
-    const int64_t target = pl.tc ? kNumSMs : 4LL * kNumSMs;
-    splits = (int)((target + base - 1) / base);
+    // Tensor-memory CTAs fill an SM each: one wave of at most 148.  The
+    // small warp-MMA CTAs run several per SM: aim for about four waves.
+    splits = pl.tc ? (int)(kNumSMs / base) : (int)((4LL * kNumSMs + base - 1) / base);
   }
   if (splits > tiles) splits = tiles;
   if (splits > 256) splits = 256;
@@ -189,10 +203,12 @@ int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st)
   dim3 grid((unsigned)((rows + 3) / 4));
   if (dtype == TV_BF16) {
     if (D == 128) split_combine_kernel<__nv_bfloat16, 128><<<grid, 128, 0, st>>>(p);
-    else split_combine_kernel<__nv_bfloat16, 64><<<grid, 128, 0, st>>>(p);
+    else if (D == 64) split_combine_kernel<__nv_bfloat16, 64><<<grid, 128, 0, st>>>(p);
+    else split_combine_kernel<__nv_bfloat16, 32><<<grid, 128, 0, st>>>(p);
   } else {
     if (D == 128) split_combine_kernel<__half, 128><<<grid, 128, 0, st>>>(p);
-    else split_combine_kernel<__half, 64><<<grid, 128, 0, st>>>(p);
+    else if (D == 64) split_combine_kernel<__half, 64><<<grid, 128, 0, st>>>(p);
+    else split_combine_kernel<__half, 32><<<grid, 128, 0, st>>>(p);
   }
   return check_launch();
 }
@@ -274,6 +290,7 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
   p.aux_sb = a->aux_sb; p.aux_sm = a->aux_sm; p.aux_sh = a->aux_sh;
   p.weight = a->weight;
   p.w_sb = a->w_sb; p.w_sm = a->w_sm; p.w_sh = a->w_sh;
+  p.err = a->status;
   if (pl.splits > 1) {
     const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
     const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);
@@ -281,7 +298,11 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
     p.part_lse = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + ((o + 255) & ~size_t(255)));
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int rc = pl.tc ? launch_attn_tc(p, a->dtype, a->head_dim, st) : launch_attn_mma(p, a->dtype, a->head_dim, st);
+  // Short key ranges take the split-P PV product (see attn_mma.cu); long ones
+  // average the bf16 rounding of P away.  Bit 4 of `kernel` forces it.
+  const bool precise = (a->kernel & 16) || a->num_keys <= kPreciseMaxKeys;
+  int rc = pl.tc ? launch_attn_tc(p, a->dtype, a->head_dim, st)
+                 : launch_attn_mma(p, a->dtype, a->head_dim, precise, st);
   if (rc != TV_OK) return rc;
   if (pl.splits > 1) rc = launch_split_combine(p, a->dtype, a->head_dim, st);
   return rc;

@@ -7,8 +7,9 @@
 
 namespace tv {
 
-// Warp-MMA (mma.sync) path: any row count, head_dim 64 or 128.
-int launch_attn_mma(const AttnParams& p, int dtype, int D, cudaStream_t st);
+// Warp-MMA (mma.sync) path: any row count, head_dim 32, 64 or 128.
+// precise: softmax weights enter PV as a hi + lo 16-bit pair.
+int launch_attn_mma(const AttnParams& p, int dtype, int D, bool precise, cudaStream_t st);
 int mma_tile_keys();
 int mma_rows_per_cta();
 

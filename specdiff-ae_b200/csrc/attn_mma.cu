@@ -73,7 +73,19 @@ __device__ __forceinline__ void load_kv_tile(const AttnParams& p, uint8_t* sK, u
   }
 }
 
-template <typename T, int D, bool PAGED>
+// Split p into a pair of 16-bit values whose sum carries ~16 more mantissa bits.
+template <typename T>
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = Elem<T>::pack2(a, b);
+  const T* h = reinterpret_cast<const T*>(&hi);
+  lo = Elem<T>::pack2(a - Elem<T>::to_f(h[0]), b - Elem<T>::to_f(h[1]));
+}
+
+// PRECISE: the softmax weights enter the PV product as a hi + lo pair of
+// 16-bit values (two MMAs) instead of one rounded value.  Rounding P to bf16
+// alone costs up to 2^-9 * max|v| of absolute error per output, which matters
+// when a row sees few keys; the pair brings it to ~2^-17.
+template <typename T, int D, bool PAGED, bool PRECISE>
 __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) {
   using G = Geo<D>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -239,11 +251,18 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
     // ---- O += P V ------------------------------------------------------------
 #pragma unroll
     for (int kk = 0; kk < BN / 16; ++kk) {
-      uint32_t a[4];
-      a[0] = Elem<T>::pack2(s[2 * kk][0], s[2 * kk][1]);
-      a[1] = Elem<T>::pack2(s[2 * kk][2], s[2 * kk][3]);
-      a[2] = Elem<T>::pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      a[3] = Elem<T>::pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      uint32_t a[4], al[4];
+      if (PRECISE) {
+        split_pair<T>(s[2 * kk][0], s[2 * kk][1], a[0], al[0]);
+        split_pair<T>(s[2 * kk][2], s[2 * kk][3], a[1], al[1]);
+        split_pair<T>(s[2 * kk + 1][0], s[2 * kk + 1][1], a[2], al[2]);
+        split_pair<T>(s[2 * kk + 1][2], s[2 * kk + 1][3], a[3], al[3]);
+      } else {
+        a[0] = Elem<T>::pack2(s[2 * kk][0], s[2 * kk][1]);
+        a[1] = Elem<T>::pack2(s[2 * kk][2], s[2 * kk][3]);
+        a[2] = Elem<T>::pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        a[3] = Elem<T>::pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      }
 #pragma unroll
       for (int dd = 0; dd < D / 16; ++dd) {
         const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
@@ -252,6 +271,10 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
         ldsm_x4_t(smem_u32(tV + G::swz(row, c)), b0, b1, b2, b3);
         Mma<T>::run(o[2 * dd], a, b0, b1);
         Mma<T>::run(o[2 * dd + 1], a, b2, b3);
+        if (PRECISE) {
+          Mma<T>::run(o[2 * dd], al, b0, b1);
+          Mma<T>::run(o[2 * dd + 1], al, b2, b3);
+        }
       }
     }
     __syncthreads();
@@ -301,10 +324,10 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
   }
 }
 
-template <typename T, int D, bool PAGED>
+template <typename T, int D, bool PAGED, bool PRECISE>
 int launch_t(const AttnParams& p, cudaStream_t st) {
   constexpr int smem = Geo<D>::SMEM;
-  auto kern = attn_mma_kernel<T, D, PAGED>;
+  auto kern = attn_mma_kernel<T, D, PAGED, PRECISE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return record_cuda_error(e);
   dim3 grid((p.R + BM - 1) / BM, p.B * p.Hkv, p.splits);
@@ -312,12 +335,19 @@ int launch_t(const AttnParams& p, cudaStream_t st) {
   return check_launch();
 }
 
-template <typename T>
-int launch_dtype(const AttnParams& p, int D, cudaStream_t st) {
+template <typename T, int D>
+int launch_d(const AttnParams& p, bool precise, cudaStream_t st) {
   const bool paged = p.pt != nullptr;
+  if (precise) return paged ? launch_t<T, D, true, true>(p, st) : launch_t<T, D, false, true>(p, st);
+  return paged ? launch_t<T, D, true, false>(p, st) : launch_t<T, D, false, false>(p, st);
+}
+
+template <typename T>
+int launch_dtype(const AttnParams& p, int D, bool precise, cudaStream_t st) {
   switch (D) {
-    case 64: return paged ? launch_t<T, 64, true>(p, st) : launch_t<T, 64, false>(p, st);
-    case 128: return paged ? launch_t<T, 128, true>(p, st) : launch_t<T, 128, false>(p, st);
+    case 32: return launch_d<T, 32>(p, precise, st);
+    case 64: return launch_d<T, 64>(p, precise, st);
+    case 128: return launch_d<T, 128>(p, precise, st);
     default: return TV_ERR_UNSUPPORTED;
   }
 }
@@ -327,9 +357,9 @@ int launch_dtype(const AttnParams& p, int D, cudaStream_t st) {
 int mma_tile_keys() { return BN; }
 int mma_rows_per_cta() { return BM; }
 
-int launch_attn_mma(const AttnParams& p, int dtype, int D, cudaStream_t st) {
-  if (dtype == TV_BF16) return launch_dtype<__nv_bfloat16>(p, D, st);
-  if (dtype == TV_F16) return launch_dtype<__half>(p, D, st);
+int launch_attn_mma(const AttnParams& p, int dtype, int D, bool precise, cudaStream_t st) {
+  if (dtype == TV_BF16) return launch_dtype<__nv_bfloat16>(p, D, precise, st);
+  if (dtype == TV_F16) return launch_dtype<__half>(p, D, precise, st);
   return TV_ERR_DTYPE;
 }
 

@@ -38,6 +38,7 @@ struct AttnParams {
   // split partials: [splits][B*Hkv][R][D] and [splits][B*Hkv][R]
   float* part_o;
   float* part_lse;
+  int* err;                // optional device status word (nonzero = a wait gave up)
 };
 
 }  // namespace tv

@@ -51,7 +51,7 @@ class AttnArgs(ctypes.Structure):
         ("aux_lse", c_vp), ("aux_sb", c_i64), ("aux_sm", c_i64), ("aux_sh", c_i64),
         ("weight", c_vp), ("w_sb", c_i64), ("w_sm", c_i64), ("w_sh", c_i64),
         ("num_splits", c_i32), ("kernel", c_i32),
-        ("workspace", c_vp), ("workspace_bytes", c_size),
+        ("workspace", c_vp), ("workspace_bytes", c_size), ("status", c_vp),
     ]
 
 

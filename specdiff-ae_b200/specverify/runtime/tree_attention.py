@@ -129,7 +129,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               weight_strides: Optional[Tuple[int, int, int]] = None,
               scale: Optional[float] = None,
               num_splits: int = 0,
-              kernel: int = 0) -> torch.Tensor:
+              kernel: int = 0,
+              status: Optional[torch.Tensor] = None) -> torch.Tensor:
     """General verify attention (see ``tv_verify_attn`` in include/specverify.h).
 
     q: [B, M, H, D]; k/v: contiguous ``[B, N, Hkv, D]`` views, or a paged pool
@@ -137,7 +138,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     ``mask_len`` keys of each sequence are gated by ``mask_bits``
     (``[B, M, words]`` uint64 as int64).  ``lse``/``aux_lse``/``weight`` are
     addressed as ``[b, m, h]`` through the given strides (default: their
-    own ``[B, M, H]`` strides).  Returns ``out``.
+    own ``[B, M, H]`` strides).  ``status`` (int32 [1], zeroed by the caller)
+    receives a nonzero code if a kernel had to abandon a bounded wait.
+    Returns ``out``.
     """
     dev = _lib.require_cuda(q, k, v, page_table, kv_lens, mask_bits, out, lse, aux_lse, weight)
     if q.dim() != 4 or q.stride(3) != 1:
@@ -214,6 +217,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         a.w_sb, a.w_sm, a.w_sh = weight_strides or weight.stride()[:3]
     a.num_splits = int(num_splits)
     a.kernel = int(kernel)
+    if status is not None:
+        if status.dtype != torch.int32 or not status.is_cuda:
+            raise _lib.SpecVerifyError(-2, "status must be a CUDA int32 tensor")
+        a.status = status.data_ptr()
     lib = _lib.load()
     need = ctypes.c_size_t(0)
     _lib.check(lib.tv_attn_workspace_size(ctypes.byref(a), ctypes.byref(need)), "tv_attn_workspace_size")
