@@ -10,6 +10,9 @@
 namespace tv {
 
 static thread_local std::string g_last_cuda_error;
+static long long* g_trace = nullptr;   // profiling aid: per-tile timestamps of CTA 0
+
+extern "C" void tv_debug_set_trace(long long* device_buffer) { g_trace = device_buffer; }
 
 int record_cuda_error(cudaError_t e) {
   g_last_cuda_error = cudaGetErrorString(e);
@@ -165,12 +168,11 @@ Plan plan(const tv_attn_args* a) {
   // The tensor-memory kernel takes long, uniform-length key ranges whose last
   // TMA box ends on a page / tile boundary (keys past the end are then whole
   // out-of-range boxes, which TMA fills with zeros).
-  const int box = paged ? (a->page_size < 128 ? a->page_size : 128) : 1;
+  const int box = paged ? (a->page_size < tc_tile_keys() ? a->page_size : tc_tile_keys()) : 1;
   pl.tc = (sel != 1) && !(a->kernel & 16) && !a->kv_lens && a->num_keys > kPreciseMaxKeys &&
           (a->num_keys % box) == 0 && tc_supported(a->dtype, D, R, paged, shift);
   pl.tile = pl.tc ? tc_tile_keys() : mma_tile_keys();
-  const int rows_per_cta = pl.tc ? tc_rows_per_cta() : mma_rows_per_cta();
-  const int row_blocks = (R + rows_per_cta - 1) / rows_per_cta;
+  const int row_blocks = pl.tc ? tc_row_blocks(R) : (R + mma_rows_per_cta() - 1) / mma_rows_per_cta();
   const int64_t base = (int64_t)row_blocks * a->batch * a->kv_heads;
   const int tiles = (a->num_keys + pl.tile - 1) / pl.tile;
   int splits = a->num_splits;
@@ -291,6 +293,7 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
   p.weight = a->weight;
   p.w_sb = a->w_sb; p.w_sm = a->w_sm; p.w_sh = a->w_sh;
   p.err = a->status;
+  p.trace = g_trace;
   if (pl.splits > 1) {
     const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
     const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);

@@ -18,6 +18,7 @@ int launch_attn_tc(const AttnParams& p, int dtype, int D, cudaStream_t st);
 bool tc_supported(int dtype, int D, int R, bool paged, int page_shift);
 int tc_tile_keys();
 int tc_rows_per_cta();
+int tc_row_blocks(int R);   // CTAs per (batch, KV head); pairs above 128 rows
 
 // Log-sum-exp merge of split partials into the final outputs of AttnParams.
 int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st);

@@ -1,35 +1,40 @@
 // Verify attention, tensor-memory path: tcgen05 MMA with TMEM accumulators,
 // TMA page-tile loads, warp-specialised (sm_100a).
 //
-// One CTA holds up to 256 query rows of one (batch, KV head) -- every tree
-// node times every query head of the GQA group -- so each 128-key K/V tile
-// is read from HBM once for all of them, and streams one split of the keys.
+// A CTA holds 128 query rows of one (batch, KV head) -- tree nodes times the
+// query heads of the GQA group -- and streams one split of the keys in
+// 128-key tiles.  Groups of more than 128 rows run as CTA pairs (a cluster
+// of two, tcgen05 cta_group::2, M = 256): each CTA loads only its half of
+// every K tile (64 keys) and of every V tile (64 head-dim columns), and one
+// MMA spans both CTAs' rows, so each K/V byte crosses from L2 to an SM once
+// and the TMA work per SM halves.  A single CTA (cta_group::1) loads whole
+// tiles.
 //
-//   warp 0        TMA producer: for each 128-key tile, one box per page (per
-//                 64-wide half of head_dim) straight from the paged pool via
-//                 the page table (or one box per half for a contiguous
-//                 cache) into a 2-stage ring of 128-byte-swizzled tiles.
-//                 Missing pages are fetched at an out-of-range page index,
-//                 which TMA fills with zeros.
-//   warp 1        MMA issuer (one thread): S_h = Q_h K^T (A = Q, B = K, both
-//                 from shared memory, fp32 accumulators in TMEM), then
-//                 O_h += P_h V (A = P read from TMEM, B = V from shared
-//                 memory).  tcgen05.commit arrives on mbarriers when groups
-//                 of MMAs retire.
-//   warps 2..     softmax, one warpgroup per 128-row half h: each thread owns
-//                 one query row (one TMEM lane), reads its 128 scores with
-//                 tcgen05.ld, applies the tree bitmask, updates the running
-//                 max / sum, and writes P (bf16 pairs) back over the scores.
-//                 The running max is only moved when it grows by more than
-//                 2^8, so O (in TMEM) is rescaled rarely; the final division
-//                 uses the same reference point, so the result is exact.
+//   warp 0    TMA producer, all 32 lanes: lane j issues the boxes of page j
+//             (one box per page and 64-wide half of head_dim, straight from
+//             the paged pool through the page table; one box per half for a
+//             contiguous cache) into K and V rings of 128-byte-swizzled
+//             tiles.  Page ids are read a tile ahead.  Missing pages are
+//             fetched at an out-of-range page index, which TMA fills with
+//             zeros.  K and V have independent cursors.
+//   warps 11, 1  MMA issuers (one thread each, in the pair's first CTA):
+//             S = Q K^T (A = Q, B = K from shared memory, fp32 accumulator in
+//             TMEM) and O += P V (A = P read from TMEM, B = V from shared
+//             memory), each issued as soon as its inputs are ready.
+//   warps 2-9 softmax: two warps per TMEM lane quarter; each thread owns one
+//             query row (one TMEM lane) and 64 of the tile's 128 key columns.
+//             The two warps exchange row maxima through shared memory; the
+//             bitmask applies on the tail tiles only; the running max only
+//             moves when it grows by more than 2^8, so O is rescaled rarely.
+//             P (16-bit pairs) is written over the scores.
 //
-// TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,384) O_1 [384,512)
-// (one half: S_0 [0,128) O_0 [128,256)).  The two halves ping-pong: while a
-// warpgroup works on S_0 the tensor core computes S_1, and so on.
+// S is triple-buffered in TMEM (S0 S1 S2 O, 128 columns each): S(j) reuses
+// the buffer of P(j-3) once PV(j-3) retired, so S runs ahead of the softmax
+// and the softmax warps never wait on their own PV.
 //
 // Every mbarrier wait is bounded (2 s); on expiry the CTA raises an abort
-// flag, records an error word, unwinds and frees its tensor memory.
+// flag (in both CTAs of a pair), records a status word, poisons its rows with
+// NaN, unwinds and frees its tensor memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -45,42 +50,126 @@ namespace {
 using namespace sm100;
 
 constexpr int BN = 128;               // keys per tile
-constexpr int HALF = 128;             // query rows per MMA (M)
+constexpr int ROWS = 128;             // query rows per CTA
 constexpr int HD = 128;               // head_dim
-constexpr int STAGES = 2;
-constexpr int SUB = 128 * 128;        // one [128 rows][64 elems] swizzled subtile (16 KB)
+constexpr int SUB = 128 * 128;        // [128 rows][64 dims] swizzled subtile (16 KB)
 constexpr int TILE = 2 * SUB;         // 128 rows x 128 dims (32 KB)
+constexpr int RING = 6 * TILE;        // shared memory of the K and V rings
 constexpr float kRescale = 8.0f;      // log2 units
+constexpr int MAXST = 6;              // most ring slots
+constexpr int THREADS = 384;          // K producer, PV issuer, 8 softmax warps, V producer, S issuer
+constexpr int SBUF = 3;               // S / P buffers in TMEM
+constexpr uint32_t TMEM_COLS = 512;   // S0 S1 S2 O, 128 columns each
+constexpr uint32_t O_COL = SBUF * BN;
+constexpr bool kUsePairs = false;   // CTA pairs: the S MMA's cross-SM K reads are slow
 
-template <int NH>
-struct Layout {
+// Per-CTA share of the K and V tiles: a pair splits K by keys and V by
+// head-dim columns.
+template <bool PAIR>
+struct Cfg {
+  static constexpr int KROWS = PAIR ? 64 : 128;    // keys of each K tile held here
+  static constexpr int VCOLS = PAIR ? 64 : 128;    // head-dim columns of each V tile held here
+  static constexpr int KSUB = KROWS * 128;         // one 64-dim half of a K slot
+  static constexpr int KSLOT = 2 * KSUB;
+  static constexpr int VSLOT = BN * VCOLS * 2;
+  static constexpr int KST = RING / 2 / KSLOT;     // 3 or 6
+  static constexpr int VST = RING / 2 / VSLOT;
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = NH * TILE;
-  static constexpr int V_OFF = K_OFF + STAGES * TILE;
-  static constexpr int BAR_OFF = V_OFF + STAGES * TILE;
-  static constexpr int SMEM = BAR_OFF + 256 + 1024;   // barriers + alignment slack
-  static constexpr int THREADS = 64 + NH * 128;
-  static constexpr uint32_t TMEM_COLS = NH == 2 ? 512 : 256;
+  static constexpr int K_OFF = TILE;
+  static constexpr int V_OFF = K_OFF + KST * KSLOT;
+  static constexpr int BAR_OFF = V_OFF + VST * VSLOT;
+  static constexpr int SMEM = BAR_OFF + 3072;      // barriers, page ids, row-max exchange
+  static constexpr uint32_t M = PAIR ? 256 : 128;  // MMA rows (both CTAs of a pair)
+  static_assert(KST <= MAXST && VST <= MAXST, "ring depth");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 struct Bars {
-  uint64_t kv_full[STAGES];
-  uint64_t kv_empty[STAGES];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t k_full[MAXST];   // pair: only the first CTA's are used
+  uint64_t k_empty[MAXST];
+  uint64_t v_full[MAXST];
+  uint64_t v_empty[MAXST];
+  uint64_t s_full[SBUF];
+  uint64_t p_full[SBUF];    // 4 softmax warps per CTA arrive (pair: on the first CTA's)
+  uint64_t pv_done[SBUF];   // per S buffer: PV of the tile in it retired
   uint64_t o_done;
+  uint64_t pair[4];         // per TMEM lane quarter: the two softmax warps meet at the end
+  uint64_t ref_bar[4];      // per quarter: one phase per tile, the reference max is published
   uint32_t tmem;
   int abort;
+  float mref[ROWS];         // reference max (log2 units) after the latest decided tile
+  float xm[2 * ROWS];       // final references and partial sums of the two warps of a row
+  float xl[2 * ROWS];
 };
+static_assert(sizeof(Bars) <= 3072, "barrier block");
 
+template <bool PAIR>
 __device__ __forceinline__ void raise_abort(Bars* bars, int* err, int code) {
   bars->abort = 1;
+  if (PAIR) st_cluster_u32(&bars->abort, cluster_rank() ^ 1u, 1u);
   if (err) atomicExch(err, code);
 }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
   return Elem<T>::pack2(lo, hi);
+}
+
+// Low / high 32-bit words of a 128-byte-swizzle shared-memory descriptor
+// (start address and leading byte offset in the low word; stride byte offset,
+// version 1 and the layout type in the high word).
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t desc_hi(uint32_t sbo_bytes) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+
+__device__ __forceinline__ void mma_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "mov.b64 ad, {%1, %2};\n\t"
+      "mov.b64 bd, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 bd;\n\t"
+      "mov.b64 bd, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The same two MMAs issued for a CTA pair (cta_group::2, M = 256): A rows and
+// the B operand's N columns are split between the two CTAs at equal shared
+// memory offsets, D lands in each CTA's tensor memory for its own rows.
+__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "mov.b64 ad, {%1, %2};\n\t"
+      "mov.b64 bd, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 bd;\n\t"
+      "mov.b64 bd, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], bd, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // Visibility of the 32 keys rel0 .. rel0+31, counted from the start of the
@@ -101,28 +190,100 @@ __device__ __forceinline__ uint32_t keep_bits(const uint64_t* mrow, int rel0, in
   return k;
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
+// Maximum over 64 scores (masked keys skipped); eight independent chains keep
+// the dependent path short for a single warp per scheduler.
+template <bool MASKED>
+__device__ __forceinline__ float chunk_max(const uint32_t* v, const uint32_t* keep) {
+  float mx[8];
+#pragma unroll
+  for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 64; ++j) {
+    float a = __uint_as_float(v[j]);
+    if (MASKED && !((keep[j >> 5] >> (j & 31)) & 1u)) a = -INFINITY;
+    mx[j & 7] = fmaxf(mx[j & 7], a);
+  }
+  return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
 }
 
-template <typename T, int NH, bool PAGED>
-__global__ void __launch_bounds__(Layout<NH>::THREADS, 1)
+// Every kPolyEvery-th pair of scores takes a polynomial 2^x on the FMA pipe
+// instead of the MUFU ex2 (0 = never): the MUFU unit (16 lanes per clock per
+// SM) is as busy as the tensor pipe on a 128-key tile otherwise.
+#ifndef TV_POLY_EVERY
+#define TV_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = TV_POLY_EVERY;
+
+// P = exp2(s * sl2 - mu) for 64 scores, packed as 16-bit pairs (key 2k in the
+// low half of word k: the layout the PV MMA reads A from); returns sum of P.
+template <typename T, bool MASKED>
+__device__ __forceinline__ float chunk_exp(const uint32_t* v, const uint32_t* keep, float sl2, float mu, uint32_t* pk) {
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 64; j += 2) {
+    float p0, p1;
+    if (kPolyEvery > 0 && ((j >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
+      const float2 e = exp2_poly2(make_float2(fmaf(__uint_as_float(v[j]), sl2, -mu), fmaf(__uint_as_float(v[j + 1]), sl2, -mu)));
+      p0 = e.x;
+      p1 = e.y;
+    } else {
+      p0 = fast_exp2(fmaf(__uint_as_float(v[j]), sl2, -mu));
+      p1 = fast_exp2(fmaf(__uint_as_float(v[j + 1]), sl2, -mu));
+    }
+    if (MASKED) {
+      const uint32_t kb = keep[j >> 5];
+      if (!((kb >> (j & 31)) & 1u)) p0 = 0.f;
+      if (!((kb >> ((j + 1) & 31)) & 1u)) p1 = 0.f;
+    }
+    s[(j >> 1) & 3] += p0 + p1;
+    pk[j >> 1] = pack_pair<T>(p0, p1);
+  }
+  return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+template <typename F>
+__device__ __forceinline__ bool timed_wait(long long& acc, F f) {
+  const long long c0 = clock64();
+  const bool r = f();
+  acc += clock64() - c0;
+  return r;
+}
+
+template <typename T, bool PAGED, bool PAIR>
+__global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                   int box_tok, int tok_first) {
-  using L = Layout<NH>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem + L::Q_OFF;
-  uint8_t* sK = smem + L::K_OFF;
-  uint8_t* sV = smem + L::V_OFF;
-  Bars* bars = reinterpret_cast<Bars*>(smem + L::BAR_OFF);
+                   int box, int tok_first) {
+  using C = Cfg<PAIR>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 128-byte-swizzled TMA tiles need 1 KB alignment; the budget leaves no
+  // room to realign, so an unaligned base is reported instead of used (both
+  // CTAs of a pair see the same layout and leave together).
+  if ((smem_u32(smem_raw) & 1023u) != 0) {
+    if (threadIdx.x == 0 && p.err) atomicExch(p.err, 7);
+    return;
+  }
+  uint8_t* smem = smem_raw;
+  uint8_t* sQ = smem + C::Q_OFF;
+  uint8_t* sK = smem + C::K_OFF;
+  uint8_t* sV = smem + C::V_OFF;
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::BAR_OFF);
   volatile int* abort = &bars->abort;
   int* err = p.err;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  // Profiling aid (null in normal use): per-CTA start/end times and wait
+  // totals, and per-tile event times of the first CTA.
+  const int cta_id = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  long long* cstat = (p.trace && cta_id < 1024) ? p.trace + 1024 + 4096 + cta_id * 16 : nullptr;
+  long long* trace = (p.trace && cta_id < 2) ? p.trace + (cta_id == 0 ? 0 : 1024 + 4096 + 16 * 1024) : nullptr;
+#define TV_TIMED(acc, expr) (cstat ? timed_wait(acc, [&]() { return (expr); }) : (expr))
+#define TV_TRACE(kind, i)                                        \
+  do {                                                           \
+    if (trace && (i) < 64) trace[(kind) * 64 + (i)] = clock64(); \
+  } while (0)
+  if (cstat && threadIdx.x == 0) {
+    p.trace[1024 + cta_id * 4] = (long long)global_ns();
+    p.trace[1024 + cta_id * 4 + 2] = clock64();
+  }
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -139,15 +300,22 @@ __global__ void __launch_bounds__(Layout<NH>::THREADS, 1)
   const int NT = t1 > t0 ? t1 - t0 : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+    for (int s = 0; s < MAXST; ++s) {
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
     }
-    for (int h = 0; h < 2; ++h) {
-      mbar_init(&bars->s_full[h], 1);
-      mbar_init(&bars->p_full[h], 4);
+    for (int s = 0; s < SBUF; ++s) {
+      mbar_init(&bars->s_full[s], 1);
+      mbar_init(&bars->p_full[s], PAIR ? 8 : 4);
     }
+    for (int s = 0; s < SBUF; ++s) mbar_init(&bars->pv_done[s], 1);
     mbar_init(&bars->o_done, 1);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(&bars->pair[q], 64);
+      mbar_init(&bars->ref_bar[q], 1);
+    }
     bars->abort = 0;
     mbar_fence_init();
   }
@@ -157,17 +325,22 @@ __global__ void __launch_bounds__(Layout<NH>::THREADS, 1)
       prefetch_tmap(&tmv);
     }
     __syncwarp();
-    tmem_alloc(&bars->tmem, L::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(&bars->tmem, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&bars->tmem, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
 
-  // ---- queries -> shared memory, 128-byte swizzled [half][d-half][row][64] --------
+  // ---- queries -> shared memory, 128-byte swizzled [d-half][row][64] --------
   {
     const T* qb = static_cast<const T*>(p.q);
-    for (int idx = threadIdx.x; idx < NH * HALF * 16; idx += L::THREADS) {
+    for (int idx = threadIdx.x; idx < ROWS * 16; idx += THREADS) {
       const int row = idx >> 4;
       const int c = idx & 15;
-      const int r = rb * NH * HALF + row;
+      const int r = rb * ROWS + row;
       uint4 val = make_uint4(0u, 0u, 0u, 0u);
       if (r < p.R) {
         int m, h;
@@ -175,162 +348,271 @@ __global__ void __launch_bounds__(Layout<NH>::THREADS, 1)
         val = *reinterpret_cast<const uint4*>(qb + (int64_t)b * p.q_sb + (int64_t)m * p.q_sm + (int64_t)h * p.q_sh +
                                               c * 8);
       }
-      const int half = row >> 7, rr = row & 127, dh = c >> 3, cc = c & 7;
-      *reinterpret_cast<uint4*>(sQ + half * TILE + dh * SUB + rr * 128 + ((cc ^ (rr & 7)) << 4)) = val;
+      const int dh = c >> 3, cc = c & 7;
+      *reinterpret_cast<uint4*>(sQ + dh * SUB + row * 128 + ((cc ^ (row & 7)) << 4)) = val;
     }
   }
   fence_proxy_async();
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync();   // barrier inits of both CTAs visible before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0 && NT > 0) {
-      int issued = 0;
-      for (int i = 0; i < NT; ++i) {
-        const int s = i % STAGES;
-        if (i >= STAGES && !mbar_wait(&bars->kv_empty[s], ((i / STAGES) & 1) ^ 1, abort)) {
-          raise_abort(bars, err, 1);
+  if (warp == 0 || warp == 10) {
+    // ---------------------------------------------------------------- producers
+    // Warp 0 loads K, warp 10 loads V, each with its own ring cursor.  One
+    // thread keeps about one TMA box in flight (a box costs its issuing
+    // thread roughly a memory latency), so a tile's boxes are spread over the
+    // lanes, and successive tiles rotate to the next lanes: box j of tile i
+    // goes to lane (i * n + j) mod 32, letting a warp keep two tiles in
+    // flight.  A box is one chunk of `box` tokens (a page, or 16 tokens of a
+    // larger page / contiguous cache) times one 64-wide half of head_dim.
+    // Each warp reads the page ids of the next tile's chunks a tile ahead.
+    if (NT > 0) {
+      const bool is_k = warp == 0;
+      const int nst = is_k ? C::KST : C::VST;
+      const int nch_v = BN / box;                      // chunks per tile
+      const int nch = is_k ? C::KROWS / box : nch_v;   // chunks this CTA loads
+      const int ch0 = is_k ? (int)rank * C::KROWS / box : 0;
+      const int nb = is_k ? 2 * nch : (PAIR ? 1 : 2) * nch;   // boxes per tile
+      uint64_t* full_ring = is_k ? bars->k_full : bars->v_full;
+      uint64_t* empty_ring = is_k ? bars->k_empty : bars->v_empty;
+      const CUtensorMap* map = is_k ? &tmk : &tmv;
+      uint8_t* base = is_k ? sK : sV;
+      const int slot_bytes = is_k ? C::KSLOT : C::VSLOT;
+      // page id of chunk `lane` of tile t (lanes past the tile's chunks: -1)
+      auto fetch_page = [&](int t) {
+        const int n0 = t * BN + lane * box;
+        return (PAGED && lane < nch_v && n0 < len) ? p.pt[(int64_t)b * p.pt_sb + (n0 >> p.page_shift)] : -1;
+      };
+      int cur_pg = PAGED ? fetch_page(t0) : -1;
+      const uint64_t t_start = global_ns();
+      long long c_idle = 0;
+      int i = 0;
+      bool failed = false;
+      while (i < NT) {
+        int go = 1;
+        if (i >= nst && lane == 0) {
+          go = mbar_try_wait(&empty_ring[i % nst], ((i / nst) & 1) ^ 1);
+          if (!go) {
+            const long long c0 = cstat ? clock64() : 0;
+            go = mbar_try_wait_hint(&empty_ring[i % nst], ((i / nst) & 1) ^ 1, 20000u);
+            if (cstat) c_idle += clock64() - c0;
+            if (!go && *abort) go = -1;
+            else if (!go && global_ns() - t_start > 2000000000ull) go = -2;
+          }
+        }
+        go = __shfl_sync(0xffffffffu, go, 0);
+        if (go < 0) {
+          failed = go == -2;
           break;
         }
-        if (*abort) break;
-        mbar_arrive_expect_tx(&bars->kv_full[s], 2 * TILE);
-        const int t = t0 + i;
-        uint8_t* dk = sK + s * TILE;
-        uint8_t* dv = sV + s * TILE;
-        if (PAGED) {
-          const int nbox = BN / box_tok;
-          for (int j = 0; j < nbox; ++j) {
-            const int n0 = t * BN + j * box_tok;
-            int page = p.num_pages;  // out of range: TMA fills zeros
-            if (n0 < len) {
-              const int pg = p.pt[(int64_t)b * p.pt_sb + (n0 >> p.page_shift)];
-              if (pg >= 0 && pg < p.num_pages) page = pg;
-            }
-            const int off = n0 & ((1 << p.page_shift) - 1);
-            const int c1 = tok_first ? off : hk, c2 = tok_first ? hk : off;
-#pragma unroll
-            for (int dh = 0; dh < 2; ++dh) {
-              tma_load_4d(dk + dh * SUB + j * box_tok * 128, &tmk, &bars->kv_full[s], dh * 64, c1, c2, page);
-              tma_load_4d(dv + dh * SUB + j * box_tok * 128, &tmv, &bars->kv_full[s], dh * 64, c1, c2, page);
-            }
-          }
-        } else {
-          const int n0 = t * BN;
-          const int c1 = tok_first ? n0 : hk, c2 = tok_first ? hk : n0;
-#pragma unroll
-          for (int dh = 0; dh < 2; ++dh) {
-            tma_load_4d(dk + dh * SUB, &tmk, &bars->kv_full[s], dh * 64, c1, c2, b);
-            tma_load_4d(dv + dh * SUB, &tmv, &bars->kv_full[s], dh * 64, c1, c2, b);
-          }
+        if (!go) continue;
+        const int s = i % nst;
+        if (lane == 0) {
+          if (is_k) TV_TRACE(0, i);
+          if (rank == 0) mbar_arrive_expect_tx(&full_ring[s], TILE);   // both CTAs' bytes
         }
-        issued = i + 1;
+        const int pg_now = cur_pg;
+        if (PAGED && i + 1 < NT) cur_pg = fetch_page(t0 + i + 1);
+        __syncwarp();
+        // At most 32 boxes per tile (chunks of >= 8 tokens): one per lane.
+        const int bx = (lane - ((i * nb) & 31)) & 31;
+        int c, half;
+        if (is_k || !PAIR) {
+          c = bx >> 1;
+          half = bx & 1;
+        } else {
+          c = bx;
+          half = (int)rank;
+        }
+        const int cc = (ch0 + c) & 31;
+        const int id = __shfl_sync(0xffffffffu, pg_now, cc);   // whole warp: page id of chunk cc
+        if (bx < nb) {
+          const int n0 = (t0 + i) * BN + cc * box;
+          int c1, c2, c3;
+          if (PAGED) {
+            const int off = n0 & ((1 << p.page_shift) - 1);
+            c1 = tok_first ? off : hk;
+            c2 = tok_first ? hk : off;
+            c3 = (id >= 0 && id < p.num_pages) ? id : p.num_pages;   // missing page / past the end: zeros
+          } else {
+            c1 = tok_first ? n0 : hk;
+            c2 = tok_first ? hk : n0;
+            c3 = b;
+          }
+          uint8_t* dst = base + s * slot_bytes + c * box * 128;
+          if (is_k) dst += half * C::KSUB;
+          else if (!PAIR) dst += half * SUB;
+          if (PAIR) tma_load_4d_pair(dst, map, mapa_shared(&full_ring[s], 0), half * 64, c1, c2, c3);
+          else tma_load_4d(dst, map, &full_ring[s], half * 64, c1, c2, c3);
+        }
+        ++i;
       }
-      if (*abort) {
-        // Let this CTA's loads in flight land before shared memory is released.
-        volatile int keep_waiting = 0;
-        for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
-          mbar_wait(&bars->kv_full[i % STAGES], (i / STAGES) & 1, &keep_waiting, 200000000ull);
+      if (lane == 0) {
+        if (failed) raise_abort<PAIR>(bars, err, 1);
+        if (cstat) cstat[is_k ? 3 : 6] = c_idle;
+        if (*abort && !PAIR) {
+          // Let this CTA's loads in flight land before shared memory is released.
+          volatile int keep_waiting = 0;
+          for (int j = i > nst ? i - nst : 0; j < i; ++j)
+            mbar_wait(&full_ring[j % nst], (j / nst) & 1, &keep_waiting, 200000000ull);
+        }
       }
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0 && NT > 0) {
-      const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-      const uint32_t id_s = idesc_f16(fmt, HALF, BN, 0);
-      const uint32_t id_pv = idesc_f16(fmt, HALF, HD, 1);
-      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
-      bool ok = mbar_wait(&bars->kv_full[0], 0, abort);
-      if (ok) {
-        tc_fence_after();
-        for (int h = 0; h < NH; ++h) {
-#pragma unroll 1
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t ad = smem_desc_sw128(sQa + h * TILE + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(sKa + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
-            mma_ss(tmem + h * 128, ad, bd, id_s, kk > 0);
+  } else if (warp == 1 || warp == 11) {
+    // ---------------------------------------------------------------- MMA issuers
+    // Two threads (of the pair's first CTA) feed the tensor pipe: warp 11
+    // issues S(j) = Q K^T as soon as K(j) has landed and the PV that last
+    // read its buffer (PV(j-3)) has retired; warp 1 issues O += P(i) V(i) as
+    // soon as P(i) and V(i) are ready.  Each keeps the pipe busy while the
+    // other waits.
+    if (lane == 0 && rank == 0 && NT > 0) {
+      constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+      constexpr uint32_t id_s = idesc_f16(fmt, C::M, BN, 0);
+      constexpr uint32_t id_pv = idesc_f16(fmt, C::M, HD, 1);
+      constexpr uint32_t hi_k = desc_hi(1024);        // 8-row groups 1 KB apart
+      const uint32_t q_lo = desc_lo(smem_u32(sQ), 16);
+      const uint32_t k_lo = desc_lo(smem_u32(sK), 16);
+      const uint32_t v_lo = desc_lo(smem_u32(sV), SUB);   // single CTA: d-halves 16 KB apart
+      bool ok = true;
+      long long w_k = 0, w_v = 0, w_p = 0;
+      auto commit = [&](uint64_t* bar) {
+        if (PAIR) tc_commit_pair(bar);
+        else tc_commit(bar);
+      };
+      if (warp == 11) {
+        for (int j = 0; ok && j < NT; ++j) {
+          const int sb = j % SBUF, ks = j % C::KST;
+          if (j >= SBUF && !mbar_wait(&bars->pv_done[sb], ((j - SBUF) / SBUF) & 1, abort)) {
+            ok = false;
+            break;
           }
-          tc_commit(&bars->s_full[h]);
-        }
-      }
-      for (int i = 0; ok && i < NT; ++i) {
-        const int s = i % STAGES;
-        for (int h = 0; h < NH; ++h) {
-          if (!mbar_wait(&bars->p_full[h], i & 1, abort)) {
+          if (!TV_TIMED(w_k, mbar_wait(&bars->k_full[ks], (j / C::KST) & 1, abort))) {
             ok = false;
             break;
           }
           tc_fence_after();
-#pragma unroll 1
+          TV_TRACE(1, j);
+          const uint32_t d = tmem + (uint32_t)(sb * BN);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t qo = (uint32_t)(((kk >> 2) * SUB + (kk & 3) * 32) >> 4);
+            const uint32_t ko = (uint32_t)((ks * C::KSLOT + (kk >> 2) * C::KSUB + (kk & 3) * 32) >> 4);
+            if (PAIR) mma_ss_pair(d, q_lo + qo, hi_k, k_lo + ko, hi_k, id_s, kk > 0 ? 1u : 0u);
+            else mma_ss_w(d, q_lo + qo, hi_k, k_lo + ko, hi_k, id_s, kk > 0 ? 1u : 0u);
+          }
+          commit(&bars->s_full[sb]);
+          commit(&bars->k_empty[ks]);
+          TV_TRACE(14, j);
+        }
+        if (!ok) raise_abort<PAIR>(bars, err, 2);
+        if (cstat) cstat[0] = w_k;
+      } else {
+        for (int i = 0; ok && i < NT; ++i) {
+          const int sb = i % SBUF, vs = i % C::VST;
+          const bool got_p = PAIR ? mbar_wait_cluster(&bars->p_full[sb], (i / SBUF) & 1, abort)
+                                  : TV_TIMED(w_p, mbar_wait(&bars->p_full[sb], (i / SBUF) & 1, abort));
+          if (!got_p) {
+            ok = false;
+            break;
+          }
+          TV_TRACE(2, i);
+          if (!TV_TIMED(w_v, mbar_wait(&bars->v_full[vs], (i / C::VST) & 1, abort))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = tmem + (uint32_t)(sb * BN);
+#pragma unroll
           for (int kb = 0; kb < BN / 16; ++kb) {
-            const uint64_t bd = smem_desc_sw128(sVa + s * TILE + kb * 2048, SUB, 1024);
-            mma_ts(tmem + NH * 128 + h * 128, tmem + h * 128 + kb * 8, bd, id_pv, (i > 0 || kb > 0) ? 1u : 0u);
+            const uint32_t vo = (uint32_t)((vs * C::VSLOT + kb * 2048) >> 4);
+            const uint32_t acc = (i > 0 || kb > 0) ? 1u : 0u;
+            if (PAIR) mma_ts_pair(tmem + O_COL, a + kb * 8, v_lo + vo, hi_k, id_pv, acc);
+            else mma_ts_w(tmem + O_COL, a + kb * 8, v_lo + vo, hi_k, id_pv, acc);
           }
-          if (h == NH - 1) tc_commit(&bars->kv_empty[s]);
-          if (i + 1 < NT) {
-            const int s2 = (i + 1) % STAGES;
-            if (h == 0) {
-              if (!mbar_wait(&bars->kv_full[s2], ((i + 1) / STAGES) & 1, abort)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-            }
-#pragma unroll 1
-            for (int kk = 0; kk < HD / 16; ++kk) {
-              const uint64_t ad = smem_desc_sw128(sQa + h * TILE + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = smem_desc_sw128(sKa + s2 * TILE + (kk >> 2) * SUB + (kk & 3) * 32, 16, 1024);
-              mma_ss(tmem + h * 128, ad, bd, id_s, kk > 0);
-            }
-            tc_commit(&bars->s_full[h]);
-          }
+          commit(&bars->v_empty[vs]);
+          commit(&bars->pv_done[sb]);
+          TV_TRACE(3, i);
+        }
+        if (ok) commit(&bars->o_done);   // tracks every PV; each followed its S
+        else raise_abort<PAIR>(bars, err, 2);
+        if (cstat) {
+          cstat[1] = w_v;
+          cstat[2] = w_p;
         }
       }
-      tc_commit(&bars->o_done);
-      if (!ok) raise_abort(bars, err, 2);
     }
-  } else {
+  } else if (warp >= 2 && warp < 10) {
     // ---------------------------------------------------------------- softmax
-    const int h = (warp - 2) >> 2;
+    // Warps 2-5 take the even tiles, warps 6-9 the odd tiles (tile i in S
+    // buffer i % 3), so the two warps sharing a scheduler (and its MUFU unit)
+    // work on successive tiles at the same time.  Warp w covers TMEM lane quarter w % 4: each
+    // thread owns one query row and all 128 keys of its tiles.  The running
+    // reference max passes from tile to tile through shared memory (one
+    // mbarrier phase per tile and quarter); it only moves when a tile's max
+    // exceeds it by more than 2^8, and then O is rescaled before that tile's
+    // PV.  Each warp keeps a partial row sum against the reference it last
+    // saw; the two are combined at the end.
     const int q4 = warp & 3;                      // TMEM lane quarter of this warp
-    const int rr = q4 * 32 + lane;                // row within the half
-    const int r = rb * NH * HALF + h * HALF + rr;
+    const int par = (warp - 2) >> 2;              // parity of the tiles this warp takes
+    const int rr = q4 * 32 + lane;                // row within the CTA
+    const int r = rb * ROWS + rr;
     const bool valid = r < p.R;
     const int m = (valid ? r : p.R - 1) / p.G;
     const uint64_t* mrow = p.mask ? p.mask + (int64_t)b * p.mask_sb + (int64_t)m * p.mask_sm : nullptr;
     const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
-    const uint32_t s_addr = lane_base + h * 128;
-    const uint32_t o_addr = lane_base + NH * 128 + h * 128;
+    const uint32_t o_addr = lane_base + O_COL;
     const float sl2 = p.scale_log2;
     const int mlen = p.mask_len;
+    uint64_t* ref_bar = &bars->ref_bar[q4];
+    uint64_t* pair = &bars->pair[q4];             // both warps of the quarter meet once, at the end
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    uint32_t v[32];
-    for (int i = 0; i < NT; ++i) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[h], i & 1, abort))) {
-        raise_abort(bars, err, 3);
+    long long w_s = 0, w_o = 0;
+    for (int i = par; i < NT; i += 2) {
+      if (!__all_sync(0xffffffffu, TV_TIMED(w_s, mbar_wait(&bars->s_full[i % SBUF], (i / SBUF) & 1, abort)))) {
+        raise_abort<PAIR>(bars, err, 3);
         ok = false;
         break;
       }
       tc_fence_after();
+      if (lane == 0 && warp == 2) TV_TRACE(4, i);
+      const uint32_t s_addr = lane_base + (uint32_t)((i % SBUF) * BN);
       const int n0 = (t0 + i) * BN;
+      // Tiles wholly inside the prefix take the unmasked path; the bitmask is
+      // applied only where the tail begins.
       const bool edge = (n0 + BN > len) || (n0 + BN > tail);
-      // Pass 1: row maximum over the tile (masked keys excluded).
       uint32_t keep[4] = {~0u, ~0u, ~0u, ~0u};
       if (edge) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) keep[c] = keep_bits(mrow, n0 + 32 * c - tail, mlen);
       }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(s_addr + 32 * c, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if ((keep[c] >> j) & 1u) mx = fmaxf(mx, __uint_as_float(v[j]));
+      // Two passes of 64 columns (three warps share a scheduler's registers,
+      // so a thread cannot hold all 128 scores): the row max, then P.
+      uint32_t v[64];
+      tmem_ld32(s_addr, v);
+      tmem_ld32(s_addr + 32, v + 32);
+      tmem_wait_ld();
+      float mx = edge ? chunk_max<true>(v, keep) : chunk_max<false>(v, keep);
+      tmem_ld32(s_addr + 64, v);
+      tmem_ld32(s_addr + 96, v + 32);
+      tmem_wait_ld();
+      mx = fmaxf(mx, edge ? chunk_max<true>(v, keep + 2) : chunk_max<false>(v, keep + 2));
+      // Reference after tile i-1 (published by the other warp of the quarter).
+      float mprev = -INFINITY;
+      if (i > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(ref_bar, (i - 1) & 1, abort))) {
+          raise_abort<PAIR>(bars, err, 6);
+          ok = false;
+          break;
+        }
+        mprev = bars->mref[rr];
+      }
+      if (mprev > m_run) {          // the reference only grows
+        l_run *= fast_exp2(m_run - mprev);
+        m_run = mprev;
       }
       const float mt = mx * sl2;
       float alpha = 1.f;
@@ -339,65 +621,102 @@ __global__ void __launch_bounds__(Layout<NH>::THREADS, 1)
         alpha = fast_exp2(m_run - mt);
         m_run = mt;
       }
-      const bool need_o = bump && l_run > 0.f;
+      bars->mref[rr] = m_run;       // reference for tile i+1
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ref_bar);
+      const bool need_o = bump && i > 0;
       if (__any_sync(0xffffffffu, need_o)) {
-        // O_h holds earlier tiles; the tensor pipe finished it before this
-        // tile's S_h (same issuing thread, in order), and the next PV into
-        // O_h waits for p_full below.
+        // O holds tiles up to i-1 scaled to mprev.  PV(i-1) is waited for on
+        // its buffer's barrier, whose previous phase (tile i-4) retired
+        // before S(i) was issued (S(i) waits for PV(i-3), and PVs retire in
+        // order), so the parity wait is exact; PV(i) waits for p_full below.
+        if (!__all_sync(0xffffffffu, TV_TIMED(w_o, mbar_wait(&bars->pv_done[(i - 1) % SBUF], ((i - 1) / SBUF) & 1, abort)))) {
+          raise_abort<PAIR>(bars, err, 4);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         const float a = need_o ? alpha : 1.f;
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          tmem_ld32(o_addr + 32 * c, v);
+          uint32_t ov[32];
+          tmem_ld32(o_addr + 32 * c, ov);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * a);
-          tmem_st32(o_addr + 32 * c, v);
+          for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * a);
+          tmem_st32(o_addr + 32 * c, ov);
         }
       }
       l_run *= alpha;
       const float mu = m_run == -INFINITY ? 0.f : m_run;
-      // Pass 2: P = exp2(s * scale * log2e - m) as bf16 pairs over the scores.
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(s_addr + 32 * c, v);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float p0 = ((keep[c] >> j) & 1u) ? fast_exp2(fmaf(__uint_as_float(v[j]), sl2, -mu)) : 0.f;
-          const float p1 = ((keep[c] >> (j + 1)) & 1u) ? fast_exp2(fmaf(__uint_as_float(v[j + 1]), sl2, -mu)) : 0.f;
-          sum0 += p0;
-          sum1 += p1;
-          pk[j >> 1] = pack_pair<T>(p0, p1);
-        }
-        tmem_st16(s_addr + 16 * c, pk);
-      }
-      l_run += sum0 + sum1;
+      // P over the scores: keys 0-63 land in columns 0-31 (read before they
+      // are overwritten), keys 64-127 in columns 32-63, whose scores are
+      // already in registers by then.
+      uint32_t pk[32];
+      tmem_ld32(s_addr, v);
+      tmem_ld32(s_addr + 32, v + 32);
+      tmem_wait_ld();
+      l_run += edge ? chunk_exp<T, true>(v, keep, sl2, mu, pk) : chunk_exp<T, false>(v, keep, sl2, mu, pk);
+      tmem_ld32(s_addr + 64, v);
+      tmem_ld32(s_addr + 96, v + 32);
+      tmem_wait_ld();
+      tmem_st32(s_addr, pk);
+      l_run += edge ? chunk_exp<T, true>(v, keep + 2, sl2, mu, pk) : chunk_exp<T, false>(v, keep + 2, sl2, mu, pk);
+      tmem_st32(s_addr + 32, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[h]);
+      if (lane == 0) TV_TRACE(6 + warp - 2, i);
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(mapa_shared(&bars->p_full[i % SBUF], 0));
+        else mbar_arrive(&bars->p_full[i % SBUF]);
+      }
+    }
+    if (cstat && lane == 0 && warp == 2) {
+      cstat[4] = w_s;
+      cstat[5] = w_o;
     }
     // ---- epilogue -------------------------------------------------------------
     if (ok && NT > 0 && !__all_sync(0xffffffffu, mbar_wait(&bars->o_done, 0, abort))) {
-      raise_abort(bars, err, 4);
+      raise_abort<PAIR>(bars, err, 5);
       ok = false;
     }
     tc_fence_after();
+    // Both warps' partial sums, brought to the final reference (the larger of
+    // the two, as the reference only grows); the pair barrier's only phase.
+    {
+      bars->xm[par * ROWS + rr] = m_run;
+      bars->xl[par * ROWS + rr] = l_run;
+      mbar_arrive(pair);
+      if (ok && !__all_sync(0xffffffffu, mbar_wait(pair, 0, abort))) {
+        raise_abort<PAIR>(bars, err, 6);
+        ok = false;
+      }
+      const float m2 = bars->xm[(par ^ 1) * ROWS + rr];
+      const float l2 = bars->xl[(par ^ 1) * ROWS + rr];
+      const float mf = fmaxf(m_run, m2);
+      if (mf != -INFINITY) {
+        l_run = (m_run == mf ? l_run : l_run * fast_exp2(m_run - mf)) + (m2 == mf ? l2 : l2 * fast_exp2(m2 - mf));
+        m_run = mf;
+      }
+    }
+    ok = ok && !*abort;
     const bool have = ok && NT > 0 && l_run > 0.f;
     // A CTA that gave up on a wait poisons its rows so the failure cannot pass
     // for a result; the status word says why.
     const float poison = ok ? 0.f : __int_as_float(0x7fc00000);
     const float inv = have ? 1.f / l_run : 0.f;
     const float lse = have ? (m_run + __log2f(l_run)) * kLn2 : (ok ? -INFINITY : poison);
+    const int ch = par;                           // this warp writes head-dim columns ch*64 .. +63
     int mm = 0, hh = 0;
     if (valid) row_coords(p, hk, r, mm, hh);
     float* prow = valid && p.splits > 1 ? part_o_row(p, split, bh, r, HD) : nullptr;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    const int d0 = ch * (HD / 2);
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t v[32];
       if (NT > 0) {   // warp-uniform: tcgen05.ld is a warp-collective instruction
-        tmem_ld32(o_addr + 32 * c, v);
+        tmem_ld32(o_addr + d0 + 32 * c, v);
         tmem_wait_ld();
       }
       if (valid) {
@@ -408,24 +727,40 @@ __global__ void __launch_bounds__(Layout<NH>::THREADS, 1)
           const float o2 = have ? __uint_as_float(v[j + 2]) * inv : poison;
           const float o3 = have ? __uint_as_float(v[j + 3]) * inv : poison;
           if (prow) {
-            *reinterpret_cast<float4*>(prow + 32 * c + j) = make_float4(o0, o1, o2, o3);
+            *reinterpret_cast<float4*>(prow + d0 + 32 * c + j) = make_float4(o0, o1, o2, o3);
           } else {
-            store_out_pair<T>(p, b, mm, hh, 32 * c + j, o0, o1);
-            store_out_pair<T>(p, b, mm, hh, 32 * c + j + 2, o2, o3);
+            store_out_pair<T>(p, b, mm, hh, d0 + 32 * c + j, o0, o1);
+            store_out_pair<T>(p, b, mm, hh, d0 + 32 * c + j + 2, o2, o3);
           }
         }
       }
     }
-    if (valid) {
+    if (valid && ch == 0) {
       if (prow) *part_lse_row(p, split, bh, r) = lse;
       else store_row_stats<T>(p, b, mm, hh, lse);
     }
   }
+#undef TV_TRACE
+#undef TV_TIMED
+
+  if (PAIR && *abort) {
+    // The peer's loads may still be signalling this CTA's barriers: give them
+    // time to land before the pair leaves (abort path only).
+    const uint64_t t_end = global_ns() + 200000ull;
+    while (global_ns() < t_end) {
+    }
+  }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync();
+  else __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, L::TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem, TMEM_COLS);
+    else tmem_dealloc(tmem, TMEM_COLS);
+  }
+  if (cstat && threadIdx.x == 0) {
+    p.trace[1024 + cta_id * 4 + 1] = (long long)global_ns();
+    p.trace[1024 + cta_id * 4 + 3] = clock64();
   }
 }
 
@@ -470,15 +805,27 @@ bool make_map(CUtensorMap* map, int dtype, const void* base, uint64_t ntok, uint
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, int NH, bool PAGED>
-int launch_t(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, int box_tok, int tok_first,
+template <typename T, bool PAGED, bool PAIR>
+int launch_t(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, int box, int tok_first,
              cudaStream_t st) {
-  using L = Layout<NH>;
-  auto kern = attn_tc_kernel<T, NH, PAGED>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+  using C = Cfg<PAIR>;
+  auto kern = attn_tc_kernel<T, PAGED, PAIR>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return record_cuda_error(e);
-  dim3 grid((p.R + NH * HALF - 1) / (NH * HALF), p.B * p.Hkv, p.splits);
-  kern<<<grid, L::THREADS, L::SMEM, st>>>(p, mk, mv, box_tok, tok_first);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tc_row_blocks(p.R), p.B * p.Hkv, p.splits);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, p, mk, mv, box, tok_first);
+  if (e != cudaSuccess) return record_cuda_error(e);
   return check_launch();
 }
 
@@ -491,36 +838,37 @@ bool tc_supported(int dtype, int D, int R, bool paged, int page_shift) {
   return encoder() != nullptr;
 }
 int tc_tile_keys() { return BN; }
-int tc_rows_per_cta() { return 2 * HALF; }
+int tc_rows_per_cta() { return ROWS; }
+// CTAs per (batch, KV head): a group of more than 128 rows runs as CTA pairs.
+int tc_row_blocks(int R) {
+  const int n = (R + ROWS - 1) / ROWS;
+  return kUsePairs && n > 1 ? (n + 1) & ~1 : n;
+}
 
 int launch_attn_tc(const AttnParams& p, int dtype, int D, cudaStream_t st) {
   if (D != HD) return TV_ERR_UNSUPPORTED;
   const bool paged = p.pt != nullptr;
-  const int box_tok = paged ? ((1 << p.page_shift) < BN ? (1 << p.page_shift) : BN) : BN;
+  const bool pair = kUsePairs && tc_row_blocks(p.R) > 1;
+  // 16-token boxes (or whole pages of 8): enough boxes per tile to keep
+  // every producer lane's load in flight.
+  const int box = paged && (1 << p.page_shift) < 16 ? (1 << p.page_shift) : 16;
   const bool tok_first = p.k_sn <= p.k_sh;
   if ((p.v_sn <= p.v_sh) != tok_first) return TV_ERR_UNSUPPORTED;
   CUtensorMap mk, mv;
   bool ok;
   if (paged) {
-    ok = make_map(&mk, dtype, p.k, 1u << p.page_shift, p.Hkv, p.num_pages, p.k_sn, p.k_sh, p.k_sb, box_tok, tok_first) &&
-         make_map(&mv, dtype, p.v, 1u << p.page_shift, p.Hkv, p.num_pages, p.v_sn, p.v_sh, p.v_sb, box_tok, tok_first);
+    ok = make_map(&mk, dtype, p.k, 1u << p.page_shift, p.Hkv, p.num_pages, p.k_sn, p.k_sh, p.k_sb, box, tok_first) &&
+         make_map(&mv, dtype, p.v, 1u << p.page_shift, p.Hkv, p.num_pages, p.v_sn, p.v_sh, p.v_sb, box, tok_first);
   } else {
-    ok = make_map(&mk, dtype, p.k, p.num_keys, p.Hkv, p.B, p.k_sn, p.k_sh, p.k_sb, box_tok, tok_first) &&
-         make_map(&mv, dtype, p.v, p.num_keys, p.Hkv, p.B, p.v_sn, p.v_sh, p.v_sb, box_tok, tok_first);
+    ok = make_map(&mk, dtype, p.k, p.num_keys, p.Hkv, p.B, p.k_sn, p.k_sh, p.k_sb, box, tok_first) &&
+         make_map(&mv, dtype, p.v, p.num_keys, p.Hkv, p.B, p.v_sn, p.v_sh, p.v_sb, box, tok_first);
   }
   if (!ok) return TV_ERR_UNSUPPORTED;
-  const bool two = p.R > HALF;
   const int tf = tok_first ? 1 : 0;
-  if (dtype == TV_BF16) {
-    if (paged) return two ? launch_t<__nv_bfloat16, 2, true>(p, mk, mv, box_tok, tf, st)
-                          : launch_t<__nv_bfloat16, 1, true>(p, mk, mv, box_tok, tf, st);
-    return two ? launch_t<__nv_bfloat16, 2, false>(p, mk, mv, box_tok, tf, st)
-               : launch_t<__nv_bfloat16, 1, false>(p, mk, mv, box_tok, tf, st);
-  }
-  if (paged) return two ? launch_t<__half, 2, true>(p, mk, mv, box_tok, tf, st)
-                        : launch_t<__half, 1, true>(p, mk, mv, box_tok, tf, st);
-  return two ? launch_t<__half, 2, false>(p, mk, mv, box_tok, tf, st)
-             : launch_t<__half, 1, false>(p, mk, mv, box_tok, tf, st);
+#define TV_LAUNCH(TT, PG) (pair ? launch_t<TT, PG, kUsePairs>(p, mk, mv, box, tf, st) : launch_t<TT, PG, false>(p, mk, mv, box, tf, st))
+  if (dtype == TV_BF16) return paged ? TV_LAUNCH(__nv_bfloat16, true) : TV_LAUNCH(__nv_bfloat16, false);
+  return paged ? TV_LAUNCH(__half, true) : TV_LAUNCH(__half, false);
+#undef TV_LAUNCH
 }
 
 }  // namespace tv
