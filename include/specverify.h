@@ -140,6 +140,16 @@ typedef struct tv_attn_args {
 int tv_attn_workspace_size(const tv_attn_args* args, size_t* bytes);
 int tv_verify_attn(const tv_attn_args* args, void* stream);
 
+/* tv_verify_attn without a caller workspace: no counterpart in the reference
+ * (its attention allocates its temporaries per call).  The split partials
+ * live in a fixed 24 MiB device array inside this library, so the call
+ * allocates nothing; args->workspace is ignored.  Limits: a request whose
+ * partials need more than 24 MiB (see tv_attn_workspace_size) returns
+ * TV_ERR_WORKSPACE; calls on the same device share the array and must not
+ * overlap; the first call on each device resolves the array's address and
+ * must come before any stream capture. */
+int tv_verify_attn_static(const tv_attn_args* args, void* stream);
+
 /* Merge `parts` partial attentions over disjoint key sets (split-KV or one
  * per rank of a sequence-sharded cache):
  *   parts_o   [parts][rows][head_dim] fp32, each normalised over its keys

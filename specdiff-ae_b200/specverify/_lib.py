@@ -73,6 +73,7 @@ _SIGNATURES = {
     "tv_last_cuda_error": (ctypes.c_char_p, []),
     "tv_attn_workspace_size": (c_i32, [ctypes.POINTER(AttnArgs), ctypes.POINTER(c_size)]),
     "tv_verify_attn": (c_i32, [ctypes.POINTER(AttnArgs), c_vp]),
+    "tv_verify_attn_static": (c_i32, [ctypes.POINTER(AttnArgs), c_vp]),
     "tv_merge_partials": (c_i32, [c_i32, c_i64, c_i32, c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_vp, c_vp]),
     "tv_pack_mask": (c_i32, [c_i32, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_i64, c_i64, c_vp]),
     "tv_accept_workspace_size": (c_i32, [ctypes.POINTER(AcceptArgs), ctypes.POINTER(c_size)]),
