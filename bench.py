@@ -47,10 +47,10 @@ import torch  # noqa: E402
 
 METRIC = "tree-verify attn HBM GB/s (%peak) + verified tok/s @64K ctx, 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per verify call (both kernels),
-# from the ncu capture summarised in profiles/attn_config2_ncu.md; None until
-# a capture of the current kernels exists.
-NCU_TRAFFIC_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one attn_tc_kernel launch on
+# this workload, from a full ncu capture of the current kernel (the dominant
+# kernel: 93 % of the call's device time).
+NCU_TRAFFIC_BYTES = 273_681_920
 
 
 def log(*a):
@@ -280,8 +280,9 @@ def run_ours(args, rank, world, dev):
             "unit": "GB/s",
             "frac": round(achieved_per_gpu / per_gpu_peak, 4),
             "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6.65 TB/s",
-            "traffic": NCU_TRAFFIC_BYTES,
-            "kernel": "verify attention (split-KV attention kernel + LSE merge kernel) per launch pair",
+            "traffic": NCU_TRAFFIC_BYTES if world == 1 else None,
+            "kernel": "attn_tc_kernel (93% of device time) + split_combine_kernel, timed together per call; "
+                      "traffic is attn_tc_kernel's per launch (ncu)",
             "tensor_tflops": round(flops / (ms * 1e-3) / 1e12 / world, 1),
         },
         "gpu_launches": launches_per_step * args.steps,

@@ -21,14 +21,17 @@ int record_cuda_error(cudaError_t e) {
 
 namespace {
 
-// ---- split combine: one warp per query row ----------------------------------
+// ---- split combine: D/4 threads per query row, one float4 of O each --------
+// Partials are read up to 8 splits at a time (all loads of a block in flight
+// together, they are usually still in L2) and folded with a running max, so
+// the row needs one pass.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) {
-  // Lane l owns head-dim pairs (2l, 2l+1), (2l+64, 2l+65), ...
-  constexpr int PER = D >= 64 ? D / 32 : 2;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+  constexpr int TPR = D / 4;          // threads per row
+  constexpr int RPB = 128 / TPR;      // rows per block
+  constexpr int BLK = 8;              // splits loaded together
+  const int q = threadIdx.x % TPR;
+  const int64_t row = (int64_t)blockIdx.x * RPB + threadIdx.x / TPR;
   const int64_t total = (int64_t)p.B * p.Hkv * p.R;
   if (row >= total) return;
   const int bh = (int)(row / p.R);
@@ -36,43 +39,51 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) 
   const int b = bh / p.Hkv;
   const int hk = bh - b * p.Hkv;
 
-  float mx = -INFINITY;
-  for (int s = lane; s < p.splits; s += 32) mx = fmaxf(mx, *part_lse_row(p, s, bh, r));
+  float mx = -INFINITY, wsum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < p.splits; s0 += BLK) {
+    float l[BLK];
+    float4 v[BLK];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-
-  float acc[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-  float wsum = 0.f;
-  if (mx != -INFINITY) {
-    for (int s = 0; s < p.splits; ++s) {
-      const float l = *part_lse_row(p, s, bh, r);
-      if (l == -INFINITY) continue;
-      const float w = expf(l - mx);
-      wsum += w;
-      const float* src = part_o_row(p, s, bh, r, D);
-#pragma unroll
-      for (int i = 0; i < PER; i += 2) {
-        const int d = 2 * lane + 32 * i;
-        if (d < D) {
-          const float2 v = *reinterpret_cast<const float2*>(src + d);
-          acc[i] += w * v.x;
-          acc[i + 1] += w * v.y;
-        }
+    for (int j = 0; j < BLK; ++j) {
+      const int s = s0 + j;
+      if (s < p.splits) {
+        l[j] = *part_lse_row(p, s, bh, r);
+        v[j] = *reinterpret_cast<const float4*>(part_o_row(p, s, bh, r, D) + 4 * q);
+      } else {
+        l[j] = -INFINITY;
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
+    float bm = l[0];
+#pragma unroll
+    for (int j = 1; j < BLK; ++j) bm = fmaxf(bm, l[j]);
+    const float nm = fmaxf(mx, bm);
+    if (nm == -INFINITY) continue;
+    const float sc = mx == -INFINITY ? 0.f : expf(mx - nm);
+    acc.x *= sc;
+    acc.y *= sc;
+    acc.z *= sc;
+    acc.w *= sc;
+    wsum *= sc;
+#pragma unroll
+    for (int j = 0; j < BLK; ++j) {
+      const float w = l[j] == -INFINITY ? 0.f : expf(l[j] - nm);
+      wsum += w;
+      acc.x += w * v[j].x;
+      acc.y += w * v[j].y;
+      acc.z += w * v[j].z;
+      acc.w += w * v[j].w;
+    }
+    mx = nm;
   }
   const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
   const float lse = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
   int m, h;
   row_coords(p, hk, r, m, h);
-#pragma unroll
-  for (int i = 0; i < PER; i += 2) {
-    const int d = 2 * lane + 32 * i;
-    if (d < D) store_out_pair<T>(p, b, m, h, d, acc[i] * inv, acc[i + 1] * inv);
-  }
-  if (lane == 0) store_row_stats<T>(p, b, m, h, lse);
+  store_out_pair<T>(p, b, m, h, 4 * q, acc.x * inv, acc.y * inv);
+  store_out_pair<T>(p, b, m, h, 4 * q + 2, acc.z * inv, acc.w * inv);
+  if (q == 0) store_row_stats<T>(p, b, m, h, lse);
 }
 
 template <typename T>
@@ -202,7 +213,8 @@ size_t workspace_for(const tv_attn_args* a, const Plan& pl) {
 
 int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st) {
   const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
-  dim3 grid((unsigned)((rows + 3) / 4));
+  const int64_t rows_per_block = 128 / (D / 4);
+  dim3 grid((unsigned)((rows + rows_per_block - 1) / rows_per_block));
   if (dtype == TV_BF16) {
     if (D == 128) split_combine_kernel<__nv_bfloat16, 128><<<grid, 128, 0, st>>>(p);
     else if (D == 64) split_combine_kernel<__nv_bfloat16, 64><<<grid, 128, 0, st>>>(p);
