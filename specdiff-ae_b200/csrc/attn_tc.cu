@@ -190,19 +190,23 @@ __device__ __forceinline__ uint32_t keep_bits(const uint64_t* mrow, int rel0, in
   return k;
 }
 
-// Maximum over 64 scores (masked keys skipped); eight independent chains keep
-// the dependent path short for a single warp per scheduler.
-template <bool MASKED>
-__device__ __forceinline__ float chunk_max(const uint32_t* v, const uint32_t* keep) {
+// Scores of keys the row may not see become -inf in place (their P is then
+// exp2(-inf) = 0), so the max and exp passes below have one code path; only
+// the tail tiles pay for it.
+__device__ __forceinline__ void apply_keep(uint32_t* v, const uint32_t* keep) {
+#pragma unroll
+  for (int j = 0; j < 64; ++j)
+    if (!((keep[j >> 5] >> (j & 31)) & 1u)) v[j] = 0xff800000u;
+}
+
+// Maximum over 64 scores; eight independent chains keep the dependent path
+// short.
+__device__ __forceinline__ float chunk_max(const uint32_t* v) {
   float mx[8];
 #pragma unroll
   for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < 64; ++j) {
-    float a = __uint_as_float(v[j]);
-    if (MASKED && !((keep[j >> 5] >> (j & 31)) & 1u)) a = -INFINITY;
-    mx[j & 7] = fmaxf(mx[j & 7], a);
-  }
+  for (int j = 0; j < 64; ++j) mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(v[j]));
   return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
 }
 
@@ -216,8 +220,8 @@ constexpr int kPolyEvery = TV_POLY_EVERY;
 
 // P = exp2(s * sl2 - mu) for 64 scores, packed as 16-bit pairs (key 2k in the
 // low half of word k: the layout the PV MMA reads A from); returns sum of P.
-template <typename T, bool MASKED>
-__device__ __forceinline__ float chunk_exp(const uint32_t* v, const uint32_t* keep, float sl2, float mu, uint32_t* pk) {
+template <typename T>
+__device__ __forceinline__ float chunk_exp(const uint32_t* v, float sl2, float mu, uint32_t* pk) {
   float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < 64; j += 2) {
@@ -229,11 +233,6 @@ __device__ __forceinline__ float chunk_exp(const uint32_t* v, const uint32_t* ke
     } else {
       p0 = fast_exp2(fmaf(__uint_as_float(v[j]), sl2, -mu));
       p1 = fast_exp2(fmaf(__uint_as_float(v[j + 1]), sl2, -mu));
-    }
-    if (MASKED) {
-      const uint32_t kb = keep[j >> 5];
-      if (!((kb >> (j & 31)) & 1u)) p0 = 0.f;
-      if (!((kb >> ((j + 1) & 31)) & 1u)) p1 = 0.f;
     }
     s[(j >> 1) & 3] += p0 + p1;
     pk[j >> 1] = pack_pair<T>(p0, p1);
@@ -595,11 +594,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_ld32(s_addr, v);
       tmem_ld32(s_addr + 32, v + 32);
       tmem_wait_ld();
-      float mx = edge ? chunk_max<true>(v, keep) : chunk_max<false>(v, keep);
+      if (edge) apply_keep(v, keep);
+      float mx = chunk_max(v);
       tmem_ld32(s_addr + 64, v);
       tmem_ld32(s_addr + 96, v + 32);
       tmem_wait_ld();
-      mx = fmaxf(mx, edge ? chunk_max<true>(v, keep + 2) : chunk_max<false>(v, keep + 2));
+      if (edge) apply_keep(v, keep + 2);
+      mx = fmaxf(mx, chunk_max(v));
       // Reference after tile i-1 (published by the other warp of the quarter).
       float mprev = -INFINITY;
       if (i > 0) {
@@ -656,12 +657,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_ld32(s_addr, v);
       tmem_ld32(s_addr + 32, v + 32);
       tmem_wait_ld();
-      l_run += edge ? chunk_exp<T, true>(v, keep, sl2, mu, pk) : chunk_exp<T, false>(v, keep, sl2, mu, pk);
+      if (edge) apply_keep(v, keep);
+      l_run += chunk_exp<T>(v, sl2, mu, pk);
       tmem_ld32(s_addr + 64, v);
       tmem_ld32(s_addr + 96, v + 32);
       tmem_wait_ld();
       tmem_st32(s_addr, pk);
-      l_run += edge ? chunk_exp<T, true>(v, keep + 2, sl2, mu, pk) : chunk_exp<T, false>(v, keep + 2, sl2, mu, pk);
+      if (edge) apply_keep(v, keep + 2);
+      l_run += chunk_exp<T>(v, sl2, mu, pk);
       tmem_st32(s_addr + 32, pk);
       tmem_wait_st();
       tc_fence_before();
