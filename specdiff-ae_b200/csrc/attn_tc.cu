@@ -58,9 +58,12 @@ constexpr int RING = 6 * TILE;        // shared memory of the K and V rings
 constexpr float kRescale = 8.0f;      // log2 units
 constexpr int MAXST = 6;              // most ring slots
 constexpr int THREADS = 384;          // K producer, PV issuer, 8 softmax warps, V producer, S issuer
-constexpr int SBUF = 3;               // S / P buffers in TMEM
-constexpr uint32_t TMEM_COLS = 512;   // S0 S1 S2 O, 128 columns each
-constexpr uint32_t O_COL = SBUF * BN;
+constexpr int SBUF = 2;               // S buffers in TMEM (fp32 scores, 128 columns each)
+constexpr int PBUF = 2;               // P buffers in TMEM (16-bit pairs, 64 columns each)
+constexpr uint32_t TMEM_COLS = 512;   // S0 S1 P0 P1 O
+constexpr uint32_t P_COL = SBUF * BN;
+constexpr uint32_t O_COL = P_COL + PBUF * (BN / 2);
+static_assert(O_COL + 128 == TMEM_COLS, "tensor memory layout");
 constexpr bool kUsePairs = false;   // CTA pairs: the S MMA's cross-SM K reads are slow
 
 // Per-CTA share of the K and V tiles: a pair splits K by keys and V by
@@ -90,8 +93,9 @@ struct Bars {
   uint64_t v_full[MAXST];
   uint64_t v_empty[MAXST];
   uint64_t s_full[SBUF];
-  uint64_t p_full[SBUF];    // 4 softmax warps per CTA arrive (pair: on the first CTA's)
-  uint64_t pv_done[SBUF];   // per S buffer: PV of the tile in it retired
+  uint64_t s_free[SBUF];    // the 4 softmax warps of a tile have read its scores
+  uint64_t p_full[PBUF];    // 4 softmax warps per CTA arrive (pair: on the first CTA's)
+  uint64_t pv_done[PBUF];   // per P buffer: PV of the tile in it retired
   uint64_t o_done;
   uint64_t pair[4];         // per TMEM lane quarter: the two softmax warps meet at the end
   uint64_t ref_bar[4];      // per quarter: one phase per tile, the reference max is published
@@ -231,8 +235,11 @@ __device__ __forceinline__ float chunk_exp(const uint32_t* v, float sl2, float m
       p0 = e.x;
       p1 = e.y;
     } else {
-      p0 = fast_exp2(fmaf(__uint_as_float(v[j]), sl2, -mu));
-      p1 = fast_exp2(fmaf(__uint_as_float(v[j + 1]), sl2, -mu));
+      // scale and shift two scores with one packed f32x2 FMA
+      const float2 x = fma2(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), make_float2(sl2, sl2),
+                            make_float2(-mu, -mu));
+      p0 = fast_exp2(x.x);
+      p1 = fast_exp2(x.y);
     }
     s[(j >> 1) & 3] += p0 + p1;
     pk[j >> 1] = pack_pair<T>(p0, p1);
@@ -269,9 +276,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort = &bars->abort;
   int* err = p.err;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;
-  // Profiling aid (null in normal use): per-CTA start/end times and wait
-  // totals, and per-tile event times of the first CTA.
+  // Profiling aid, compiled in only with TV_PROFILE_TRACE (and then active
+  // only when the host set a trace buffer): per-CTA start/end times and wait
+  // totals, and per-tile event times of the first CTAs.
   const int cta_id = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+#ifdef TV_PROFILE_TRACE
   long long* cstat = (p.trace && cta_id < 1024) ? p.trace + 1024 + 4096 + cta_id * 16 : nullptr;
   long long* trace = (p.trace && cta_id < 2) ? p.trace + (cta_id == 0 ? 0 : 1024 + 4096 + 16 * 1024) : nullptr;
 #define TV_TIMED(acc, expr) (cstat ? timed_wait(acc, [&]() { return (expr); }) : (expr))
@@ -279,6 +288,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   do {                                                           \
     if (trace && (i) < 64) trace[(kind) * 64 + (i)] = clock64(); \
   } while (0)
+#else
+  long long* const cstat = nullptr;
+#define TV_TIMED(acc, expr) (expr)
+#define TV_TRACE(kind, i) \
+  do {                    \
+  } while (0)
+#endif
+  (void)cta_id;
   if (cstat && threadIdx.x == 0) {
     p.trace[1024 + cta_id * 4] = (long long)global_ns();
     p.trace[1024 + cta_id * 4 + 2] = clock64();
@@ -307,9 +324,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int s = 0; s < SBUF; ++s) {
       mbar_init(&bars->s_full[s], 1);
+      mbar_init(&bars->s_free[s], PAIR ? 8 : 4);
       mbar_init(&bars->p_full[s], PAIR ? 8 : 4);
     }
-    for (int s = 0; s < SBUF; ++s) mbar_init(&bars->pv_done[s], 1);
+    for (int s = 0; s < PBUF; ++s) mbar_init(&bars->pv_done[s], 1);
     mbar_init(&bars->o_done, 1);
     for (int q = 0; q < 4; ++q) {
       mbar_init(&bars->pair[q], 64);
@@ -484,7 +502,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (warp == 11) {
         for (int j = 0; ok && j < NT; ++j) {
           const int sb = j % SBUF, ks = j % C::KST;
-          if (j >= SBUF && !mbar_wait(&bars->pv_done[sb], ((j - SBUF) / SBUF) & 1, abort)) {
+          // buffer sb is free once the softmax warps have read S(j - SBUF)
+          if (j >= SBUF && !(PAIR ? mbar_wait_cluster(&bars->s_free[sb], ((j - SBUF) / SBUF) & 1, abort)
+                                  : mbar_wait(&bars->s_free[sb], ((j - SBUF) / SBUF) & 1, abort))) {
             ok = false;
             break;
           }
@@ -510,9 +530,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (cstat) cstat[0] = w_k;
       } else {
         for (int i = 0; ok && i < NT; ++i) {
-          const int sb = i % SBUF, vs = i % C::VST;
-          const bool got_p = PAIR ? mbar_wait_cluster(&bars->p_full[sb], (i / SBUF) & 1, abort)
-                                  : TV_TIMED(w_p, mbar_wait(&bars->p_full[sb], (i / SBUF) & 1, abort));
+          const int pb = i % PBUF, vs = i % C::VST;
+          const bool got_p = PAIR ? mbar_wait_cluster(&bars->p_full[pb], (i / PBUF) & 1, abort)
+                                  : TV_TIMED(w_p, mbar_wait(&bars->p_full[pb], (i / PBUF) & 1, abort));
           if (!got_p) {
             ok = false;
             break;
@@ -523,7 +543,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a = tmem + (uint32_t)(sb * BN);
+          const uint32_t a = tmem + P_COL + (uint32_t)(pb * (BN / 2));
 #pragma unroll
           for (int kb = 0; kb < BN / 16; ++kb) {
             const uint32_t vo = (uint32_t)((vs * C::VSLOT + kb * 2048) >> 4);
@@ -532,7 +552,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             else mma_ts_w(tmem + O_COL, a + kb * 8, v_lo + vo, hi_k, id_pv, acc);
           }
           commit(&bars->v_empty[vs]);
-          commit(&bars->pv_done[sb]);
+          commit(&bars->pv_done[pb]);
           TV_TRACE(3, i);
         }
         if (ok) commit(&bars->o_done);   // tracks every PV; each followed its S
@@ -627,11 +647,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(ref_bar);
       const bool need_o = bump && i > 0;
       if (__any_sync(0xffffffffu, need_o)) {
-        // O holds tiles up to i-1 scaled to mprev.  PV(i-1) is waited for on
-        // its buffer's barrier, whose previous phase (tile i-4) retired
-        // before S(i) was issued (S(i) waits for PV(i-3), and PVs retire in
-        // order), so the parity wait is exact; PV(i) waits for p_full below.
-        if (!__all_sync(0xffffffffu, TV_TIMED(w_o, mbar_wait(&bars->pv_done[(i - 1) % SBUF], ((i - 1) / SBUF) & 1, abort)))) {
+        // O holds tiles up to i-1 scaled to mprev; PV(i-1) must retire first.
+        // PV(i-2) is waited for on this warp's own P-buffer barrier (exact:
+        // its tile i-4 phase was observed before P(i-2) was written); PVs
+        // retire in order, so the other buffer's barrier then stands at tile
+        // i-1 and that wait is exact too.  PV(i) waits for p_full below.
+        bool got = true;
+        if (i >= 2) got = mbar_wait(&bars->pv_done[i % PBUF], ((i - 2) / PBUF) & 1, abort);
+        if (got) got = TV_TIMED(w_o, mbar_wait(&bars->pv_done[(i - 1) % PBUF], ((i - 1) / PBUF) & 1, abort));
+        if (!__all_sync(0xffffffffu, got)) {
           raise_abort<PAIR>(bars, err, 4);
           ok = false;
           break;
@@ -650,9 +674,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       l_run *= alpha;
       const float mu = m_run == -INFINITY ? 0.f : m_run;
-      // P over the scores: keys 0-63 land in columns 0-31 (read before they
-      // are overwritten), keys 64-127 in columns 32-63, whose scores are
-      // already in registers by then.
+      // P: keys 0-63 into P-buffer columns 0-31, keys 64-127 into 32-63.
       uint32_t pk[32];
       tmem_ld32(s_addr, v);
       tmem_ld32(s_addr + 32, v + 32);
@@ -662,17 +684,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_ld32(s_addr + 64, v);
       tmem_ld32(s_addr + 96, v + 32);
       tmem_wait_ld();
-      tmem_st32(s_addr, pk);
+      // All of S(i) is in registers: its buffer can take S(i + SBUF).
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(mapa_shared(&bars->s_free[i % SBUF], 0));
+        else mbar_arrive(&bars->s_free[i % SBUF]);
+      }
+      // P buffer i % PBUF held P(i - 2), this warp's own previous tile, whose
+      // PV was issued right after it, so this wait rarely blocks.  Its phase
+      // for tile i - 4 completed before this warp wrote P(i - 2), so the
+      // parity wait is exact.
+      if (i >= PBUF && !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i % PBUF], ((i - PBUF) / PBUF) & 1, abort))) {
+        raise_abort<PAIR>(bars, err, 7);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t p_addr = lane_base + P_COL + (uint32_t)((i % PBUF) * (BN / 2));
+      tmem_st32(p_addr, pk);
       if (edge) apply_keep(v, keep + 2);
       l_run += chunk_exp<T>(v, sl2, mu, pk);
-      tmem_st32(s_addr + 32, pk);
+      tmem_st32(p_addr + 32, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) TV_TRACE(6 + warp - 2, i);
       if (lane == 0) {
-        if (PAIR) mbar_arrive_cluster(mapa_shared(&bars->p_full[i % SBUF], 0));
-        else mbar_arrive(&bars->p_full[i % SBUF]);
+        if (PAIR) mbar_arrive_cluster(mapa_shared(&bars->p_full[i % PBUF], 0));
+        else mbar_arrive(&bars->p_full[i % PBUF]);
       }
     }
     if (cstat && lane == 0 && warp == 2) {

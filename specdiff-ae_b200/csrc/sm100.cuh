@@ -78,6 +78,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_test_wait(bar, parity)) return true;
+#if defined(TV_SPIN_SLEEP_NS) && TV_SPIN_SLEEP_NS > 0
+    __nanosleep(TV_SPIN_SLEEP_NS);
+#endif
     if ((it & 255u) == 0) {
       if (*abort) return false;
       if (global_ns() - t0 > limit_ns) return false;
