@@ -185,11 +185,35 @@ def run_ours(args, rank, world, dev):
         workload = (f"config2 sequence-sharded over {world} GPUs: S=65536 paged, 64-node depth-8 tree, 1 layer, "
                     f"bf16, one NCCL all_gather of (O, lse) partials + LSE merge per step")
 
-    # correctness spot check of the timed configuration (rank 0 vs single-GPU call)
     for _ in range(args.warmup):
         for i in range(rotate):
             step(i)
     torch.cuda.synchronize()
+    # The timed steps replay CUDA graphs of the launch sequence (one per
+    # rotated problem; the sharded step's NCCL all_gather included), so the
+    # device time is not bounded by Python launch overhead.
+    graphs = []
+    if not args.no_graph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(rotate):
+                step(i)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        for i in range(rotate):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step(i)
+            graphs.append(g)
+        torch.cuda.synchronize()
+
+        def step(i):  # noqa: F811 -- the timed loop replays the captured steps
+            graphs[i % rotate].replay()
+
+        for i in range(rotate):
+            step(i)
+        torch.cuda.synchronize()
 
     sampler = ClockSampler(physical_gpu_index(torch.cuda.current_device()))
     if rank == 0:
@@ -214,6 +238,44 @@ def run_ours(args, rank, world, dev):
 
     # ---- end to end through the public API with host buffers -------------
     e2e = None
+    if world > 1 and not args.no_e2e:
+        # every rank: pinned host Q (and, on the tree rank, the keep mask) in,
+        # the merged output and LSE back to the host; slowest rank counts
+        q_host = [p.q.cpu().pin_memory() for p in probs]
+        keep_host = [p.tree.keep.clone().pin_memory() for p in probs]
+        out_host = [torch.empty(p.q.shape, dtype=p.q.dtype).pin_memory() for p in probs]
+        lse_host = [torch.empty(p.q.shape[:3], dtype=torch.float32).pin_memory() for p in probs]
+
+        def e2e_step(i):
+            p = probs[i % rotate]
+            q = q_host[i % rotate].to(dev, non_blocking=True)
+            keep = keep_host[i % rotate].to(dev, non_blocking=True) if rank == world - 1 else None
+            o, lse = verifier(q, p.k_pool, p.v_pool, shard_len, keep, page_table=shards[i % rotate],
+                              return_lse=True)
+            out_host[i % rotate].copy_(o, non_blocking=True)
+            lse_host[i % rotate].copy_(lse, non_blocking=True)
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        for i in range(args.steps):
+            e2e_step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1e3 / args.steps
+        t = torch.tensor([max(e0.elapsed_time(e1) / args.steps, wall)], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ems = float(t.item())
+        h2d = p0.q.numel() * p0.q.element_size() * world + p0.tree.keep.numel()
+        d2h = (p0.q.numel() * p0.q.element_size() + p0.q.shape[0] * p0.q.shape[1] * p0.q.shape[2] * 4) * world
+        e2e = {"value": round(alg_bytes / (ems * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ems, 4),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "specverify.runtime.sharded.SequenceShardedVerify (pinned host q/mask in, out/lse back "
+                      "to host on every rank)"}
     if world == 1 and not args.no_e2e:
         q_host = [p.q.cpu().pin_memory() for p in probs]
         keep_host = [p.tree.keep.clone().pin_memory() for p in probs]
@@ -247,6 +309,7 @@ def run_ours(args, rank, world, dev):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "api": "specverify.runtime.verify_attention (pinned host q/mask in, out/lse back to host)"}
 
+    graphs.clear()   # graphs holding NCCL work are released before the process group goes
     total_bytes = alg_bytes  # whole job: the full 64K problem once per step (sharded or not)
     value = total_bytes / (ms * 1e-3) / 1e9
     hbm, kind = peaks()
@@ -271,6 +334,7 @@ def run_ours(args, rank, world, dev):
             "head_dim": p0.q.shape[3], "page_size": page, "layers_rotated": rotate,
             "l2": "inputs larger than L2: 4 independent 268 MB KV pools rotated per step",
             "algorithmic_bytes_per_step": alg_bytes, "flops_per_step": flops,
+            "launch": "eager" if args.no_graph else "CUDA graph replay of each step's launches",
             "parallelism": "single GPU" if world == 1 else f"sequence-sharded x{world}",
         },
         "roofline": {
@@ -349,6 +413,9 @@ def run_reference(args, rank, world):
     }
 
 
+_JSON_OUT = sys.stdout
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -357,6 +424,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -364,10 +432,16 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # Exactly one JSON line on stdout: libraries (NCCL's version banner) that
+    # print to stdout are sent to stderr instead.
+    global _JSON_OUT
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=_JSON_OUT, flush=True)
         return
     if not torch.cuda.is_available():
         raise SystemExit("bench.py (ours) needs a CUDA device")
@@ -384,7 +458,7 @@ def main():
                 gbs, sec, thr, desc = cpu_reference_sample(8192)
                 res["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
                                        "sample": desc + f"; {sec * 1e3:.1f} ms per pass"}
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=_JSON_OUT, flush=True)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -161,6 +161,25 @@ int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
                       const float* parts_lse, int64_t part_stride_lse,
                       int32_t out_dtype, void* out, float* out_lse, void* stream);
 
+/* ---- sequence-sharded exchange over NVLink peer memory --------------------
+ * No counterpart in the reference (it has no multi-GPU verify).  Each rank's
+ * buffer, mapped into every rank, holds two partial slots
+ *   slot s at byte s * slot_bytes: O [rows][head_dim] fp32, then lse [rows]
+ * and, at flag_offset, int32 words [flag 0, flag 1, ready, finished], all
+ * zero before the first step; `counter` (this rank's step count, zero
+ * initially) is device memory of this rank.  tv_peer_merge, after this
+ * rank's partial was written on `stream`: publishes flags[slot] = step with a
+ * system-scope release, waits (bounded, 2 s; then *status = 8 and NaN rows)
+ * until every peer's flags[slot] reaches the step, merges all ranks' slot
+ * partials (read over NVLink) by log-sum-exp in rank order into
+ * out [rows][head_dim] (out_dtype) and out_lse [rows] (optional), and
+ * advances the counter.  bases[r] = rank r's buffer as mapped in this
+ * process (world <= 8).  Successive steps must alternate the slot. */
+int tv_peer_merge(int32_t world, int32_t rank, const void* const* bases, int64_t slot_bytes,
+                  int32_t slot, int64_t flag_offset, int32_t* counter, int64_t rows,
+                  int32_t head_dim, int32_t out_dtype, void* out, float* out_lse,
+                  int32_t* status, void* stream);
+
 /* ---- masks --------------------------------------------------------------
  * Pack a [batch][rows][cols] keep-mask into bits: bit c of row r is set when
  *   kind 0 (int8/uint8/bool): element != 0

@@ -5,19 +5,24 @@ The reference attends the whole prefix on one device
 contexts the prefix KV is split into contiguous, page-aligned shards, one per
 rank.  Each rank runs the verify-attention kernel over its shard -- the rank
 that owns the tree tail also applies the tree bitmask to the M tree keys --
-and writes its partial ``(O_r fp32 [B, M, H, D], lse_r [B, M, H])`` into one
-packed buffer.  ONE ``all_gather`` over NCCL (NVLink/NVSwitch) exchanges the
-packed partials, and every rank merges them locally with ``tv_merge_partials``:
+and produces its partial ``(O_r fp32 [B, M, H, D], lse_r [B, M, H])``.  The
+partials are exchanged and every rank merges them in rank order:
 
     O = sum_r e^{lse_r - L} O_r / sum_r e^{lse_r - L},   L = max_r lse_r
 
-The gather is order-fixed, so every rank gets bit-identical results (the
-next layer's replicated projections need that).  An all-reduce formulation
-would need a max-reduce first: two collectives.
+Default exchange: NVLink peer memory.  Each rank writes its partial into a
+buffer mapped into every rank (torch symmetric memory) and one kernel,
+``tv_peer_merge``, publishes it, waits for every peer's and merges all
+partials straight from the peers' memory -- no collective launch.  Fallback
+(and the host-testable form): ONE NCCL ``all_gather`` of the packed partials
+and ``tv_merge_partials``.  Both are order-fixed, so every rank gets
+bit-identical results (the next layer's replicated projections need that).
+An all-reduce formulation would need a max-reduce first: two collectives.
 """
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -77,6 +82,58 @@ def merge_packed(gathered: torch.Tensor, part: PackedPartial, world: int, out_dt
     return out
 
 
+class PeerExchange:
+    """Partials exchanged through NVLink peer memory instead of a collective.
+
+    One buffer per rank, mapped into every rank (torch symmetric memory):
+    two partial slots (successive steps alternate), two flags and a step
+    counter.  A step writes this rank's partial into its slot, then
+    ``tv_peer_merge`` publishes it, waits for every peer's flag and merges
+    all ranks' partials straight from their memory.
+    """
+
+    def __init__(self, group, b, m, h, d, device):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.shape = (b, m, h, d)
+        self.rows = b * m * h
+        self.slot_floats = -(-(self.rows * d + self.rows) // 64) * 64       # 256-byte aligned slots
+        total = 2 * self.slot_floats + 64
+        self.buf = symm.empty(total, dtype=torch.float32, device=device)
+        self.buf.zero_()                                                     # flags and counter start at 0
+        torch.cuda.synchronize(device)
+        self.handle = symm.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
+        ptrs = list(self.handle.buffer_ptrs)
+        self.bases = (ctypes.c_void_p * self.world)(*ptrs)
+        flag_floats = 2 * self.slot_floats
+        self.counter = self.buf[flag_floats + 4:flag_floats + 5].view(torch.int32)
+        self.flag_offset = flag_floats * 4
+        self.step = 0
+        dist.barrier(group)    # every rank's zeroed flags are in place before anyone waits on them
+
+    def slot(self):
+        s = self.step & 1
+        self.step += 1
+        return s
+
+    def views(self, s):
+        b, m, h, d = self.shape
+        base = s * self.slot_floats
+        o = self.buf[base:base + self.rows * d].view(b, m, h, d)
+        lse = self.buf[base + self.rows * d:base + self.rows * d + self.rows].view(b, m, h)
+        return o, lse
+
+    def merge(self, s, out, out_lse, status=None):
+        lib = _lib.load()
+        dev = out.device
+        stream = _lib.stream_ptr(dev)
+        _lib.check(lib.tv_peer_merge(self.world, self.rank, self.bases, self.slot_floats * 4, s, self.flag_offset,
+                                     self.counter.data_ptr(), self.rows, self.shape[3], _lib.dtype_code(out.dtype),
+                                     out.data_ptr(), _lib.ptr(out_lse), _lib.ptr(status), stream), "tv_peer_merge")
+
+
 class SequenceShardedVerify:
     """Verify attention over a prefix sharded across the ranks of ``group``.
 
@@ -86,13 +143,33 @@ class SequenceShardedVerify:
     exchange can be exercised with CPU ``gloo`` ranks.
     """
 
-    def __init__(self, group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None):
+    def __init__(self, group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
+                 exchange: str = "auto"):
+        """``exchange``: ``"peer"`` (NVLink peer memory, kernels only),
+        ``"nccl"`` (one all_gather), or ``"auto"`` (peer when the default
+        CUDA partial and merge are used and peer mapping succeeds)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.partial_fn = partial_fn or self._cuda_partial
         self.merge_fn = merge_fn or merge_packed
+        self.exchange = exchange
         self._bufs = {}
+        self._peer = {}
+
+    def _peer_exchange(self, b, m, h, d, device):
+        if self.exchange == "nccl" or (self.exchange == "auto" and (self.partial_fn != self._cuda_partial
+                                                                     or self.merge_fn is not merge_packed)):
+            return None
+        key = (b, m, h, d, str(device))
+        if key not in self._peer:
+            try:
+                self._peer[key] = PeerExchange(self.group, b, m, h, d, device)
+            except Exception:
+                if self.exchange == "peer":
+                    raise
+                self._peer[key] = None     # peer mapping unavailable: the all_gather path
+        return self._peer[key]
 
     def buffers(self, b, m, h, d, device):
         key = (b, m, h, d, str(device))
@@ -115,11 +192,21 @@ class SequenceShardedVerify:
         mask or packed bits) and has the M tree keys as its last ``M`` keys.
         Returns the merged output on every rank."""
         b, m, h, d = q.shape
-        part, gathered = self.buffers(b, m, h, d, q.device)
         bits, mlen = None, 0
         if tree_mask is not None:
             bits = tree_mask if tree_mask.dtype == torch.int64 else pack_tree_mask(tree_mask, batch=b)
             mlen = m
+        peer = self._peer_exchange(b, m, h, d, q.device)
+        if peer is not None:
+            s = peer.slot()
+            o_part, l_part = peer.views(s)
+            attention(q, k_shard, v_shard, num_keys=shard_len, page_table=page_table, mask_bits=bits,
+                      mask_len=mlen, out=o_part, lse=l_part, num_splits=num_splits)
+            out = torch.empty((b, m, h, d), dtype=out_dtype or q.dtype, device=q.device)
+            lse = torch.empty((b, m, h), dtype=torch.float32, device=q.device) if return_lse else None
+            peer.merge(s, out, lse)
+            return (out, lse) if return_lse else out
+        part, gathered = self.buffers(b, m, h, d, q.device)
         self.partial_fn(part, q, k_shard, v_shard, shard_len, bits, mlen, page_table, num_splits)
         dist.all_gather_into_tensor(gathered, part.buf, group=self.group)
         lse = torch.empty((b, m, h), dtype=torch.float32, device=q.device) if return_lse else None

@@ -1,0 +1,90 @@
+"""Sequence-sharded verify attention on two GPUs (skipped with fewer).
+
+Each rank attends its page-aligned shard of a paged prefix (the last rank
+also the tree keys under the bitmask) and the partials are exchanged -- over
+NVLink peer memory (the default) or one NCCL all_gather -- and merged on
+every rank.  The merged output must match the single-GPU kernel on the whole
+cache within bf16 rounding, be identical on every rank and stable over
+repeated steps (the peer path alternates its two buffer slots).
+"""
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from conftest import cuda_ok
+
+ROOT = Path(__file__).resolve().parents[1]
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir):
+    sys.path.insert(0, str(ROOT / "specdiff-ae_b200"))
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from specverify import workloads as wl
+        from specverify.runtime import attention, pack_tree_mask
+        from specverify.runtime import sharded as sh
+        w = wl.paged_verify(prefix_len=8192, nodes=64, per_depth=8, seed=3, device=dev)
+        bits = pack_tree_mask(w.tree.keep.to(dev))
+        m, page = w.tree.rows, w.page_size
+        npp = w.prefix_len // page
+        lo, hi = sh.shard_bounds(npp, world, rank)
+        last = rank == world - 1
+        tbl = w.page_table[:, lo:hi]
+        if last:
+            tbl = torch.cat([tbl, w.page_table[:, npp:]], dim=1)
+        tbl = tbl.contiguous()
+        shard_len = (hi - lo) * page + (m if last else 0)
+        ref = torch.empty_like(w.q)
+        ref_lse = torch.empty(w.q.shape[:3], device=dev)
+        attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
+                  mask_len=m, out=ref, lse=ref_lse)
+        res = {"ref": ref.cpu(), "ref_lse": ref_lse.cpu()}
+        for mode in ("peer", "nccl"):
+            ver = sh.SequenceShardedVerify(exchange=mode)
+            outs = [ver(w.q, w.k_pool, w.v_pool, shard_len, bits if last else None, page_table=tbl, return_lse=True)
+                    for _ in range(5)]
+            torch.cuda.synchronize()
+            res[mode] = [(o.cpu(), l.cpu()) for o, l in outs]
+        torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not cuda_ok() or torch.cuda.device_count() < 2, reason="needs two CUDA devices")
+@pytest.mark.timeout(600)
+def test_sharded_exchanges_match_single_gpu(tmp_path):
+    world = 2
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(world)]
+    ref, ref_lse = r[0]["ref"].float(), r[0]["ref_lse"]
+    for mode in ("peer", "nccl"):
+        first_o, first_l = r[0][mode][0]
+        for rank in range(world):
+            for o, l in r[rank][mode]:
+                assert torch.equal(o, first_o) and torch.equal(l, first_l), (mode, rank)
+        assert torch.isfinite(first_o.float()).all()
+        # two merges of fp32 partials vs the kernel's own split merge: bf16 rounding apart
+        torch.testing.assert_close(first_o.float(), ref, rtol=2e-2, atol=2e-3)
+        torch.testing.assert_close(first_l, ref_lse, rtol=1e-5, atol=1e-5)
+    # both exchanges merge the same partials with the same algebra
+    torch.testing.assert_close(r[0]["peer"][0][0].float(), r[0]["nccl"][0][0].float(), rtol=0, atol=2e-3)
