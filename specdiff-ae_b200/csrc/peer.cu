@@ -36,7 +36,7 @@ struct PeerBases {
   const char* base[8];
 };
 
-template <typename T, int D>
+template <typename T, int D, int W>
 __global__ void __launch_bounds__(128) peer_merge_kernel(PeerBases pb, int world, int rank, int64_t slot_bytes,
                                                          int slot, int64_t flag_off, int* counter, int64_t rows,
                                                          void* out, float* out_lse, int* status) {
@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(128) peer_merge_kernel(PeerBases pb, int world
       // it), then wait for every peer's; then release the other blocks.
       __threadfence_system();
       st_release_sys(my_words + slot, e);
-      for (int p = 0; p < world && ok; ++p) {
+      for (int p = 0; p < W && ok; ++p) {
         if (p == rank) continue;
         const int* flag = reinterpret_cast<const int*>(pb.base[p] + flag_off) + slot;
         unsigned it = 0;
@@ -95,25 +95,29 @@ __global__ void __launch_bounds__(128) peer_merge_kernel(PeerBases pb, int world
   float lse = -INFINITY;
   if (row >= rows) {
   } else if (ok_s) {
-    float mx = -INFINITY;
-    float l[8];
-    for (int p = 0; p < world; ++p) {
+    // All ranks' loads first (remote ones cross NVLink with ~us latency),
+    // then the merge.
+    float l[W];
+    float4 v[W];
+#pragma unroll
+    for (int p = 0; p < W; ++p) {
       const float* part = reinterpret_cast<const float*>(pb.base[p] + slot * slot_bytes);
       l[p] = __ldcg(part + rows * D + row);
-      mx = fmaxf(mx, l[p]);
+      v[p] = __ldcg(reinterpret_cast<const float4*>(part + row * D) + q);
     }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < W; ++p) mx = fmaxf(mx, l[p]);
     float wsum = 0.f;
     if (mx != -INFINITY) {
-      for (int p = 0; p < world; ++p) {
-        if (l[p] == -INFINITY) continue;
-        const float* part = reinterpret_cast<const float*>(pb.base[p] + slot * slot_bytes);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(part + row * D) + q);
-        const float w = expf(l[p] - mx);
+#pragma unroll
+      for (int p = 0; p < W; ++p) {
+        const float w = l[p] == -INFINITY ? 0.f : expf(l[p] - mx);
         wsum += w;
-        o[0] += w * v.x;
-        o[1] += w * v.y;
-        o[2] += w * v.z;
-        o[3] += w * v.w;
+        o[0] += w * v[p].x;
+        o[1] += w * v[p].y;
+        o[2] += w * v[p].z;
+        o[3] += w * v[p].w;
       }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
@@ -165,20 +169,32 @@ int tv_peer_merge(int32_t world, int32_t rank, const void* const* bases, int64_t
   const int rpb = 128 / (head_dim / 4);
   dim3 grid((unsigned)((rows + rpb - 1) / rpb));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define TV_PEER(TT, DD)                                                                                          \
-  peer_merge_kernel<TT, DD><<<grid, 128, 0, st>>>(pb, world, rank, slot_bytes, slot, flag_offset, counter, rows, \
-                                                  out, out_lse, status)
+#define TV_PEER_W(TT, DD, WW)                                                                              \
+  peer_merge_kernel<TT, DD, WW><<<grid, 128, 0, st>>>(pb, world, rank, slot_bytes, slot, flag_offset, counter, \
+                                                      rows, out, out_lse, status)
+#define TV_PEER(TT, DD)                    \
+  switch (world) {                         \
+    case 1: TV_PEER_W(TT, DD, 1); break;   \
+    case 2: TV_PEER_W(TT, DD, 2); break;   \
+    case 3: TV_PEER_W(TT, DD, 3); break;   \
+    case 4: TV_PEER_W(TT, DD, 4); break;   \
+    case 5: TV_PEER_W(TT, DD, 5); break;   \
+    case 6: TV_PEER_W(TT, DD, 6); break;   \
+    case 7: TV_PEER_W(TT, DD, 7); break;   \
+    default: TV_PEER_W(TT, DD, 8); break;  \
+  }
   if (out_dtype == TV_BF16) {
-    if (head_dim == 128) TV_PEER(__nv_bfloat16, 128);
-    else if (head_dim == 64) TV_PEER(__nv_bfloat16, 64);
-    else TV_PEER(__nv_bfloat16, 32);
+    if (head_dim == 128) TV_PEER(__nv_bfloat16, 128)
+    else if (head_dim == 64) TV_PEER(__nv_bfloat16, 64)
+    else TV_PEER(__nv_bfloat16, 32)
   } else if (out_dtype == TV_F16) {
-    if (head_dim == 128) TV_PEER(__half, 128);
-    else if (head_dim == 64) TV_PEER(__half, 64);
-    else TV_PEER(__half, 32);
+    if (head_dim == 128) TV_PEER(__half, 128)
+    else if (head_dim == 64) TV_PEER(__half, 64)
+    else TV_PEER(__half, 32)
   } else {
     return TV_ERR_DTYPE;
   }
+#undef TV_PEER_W
 #undef TV_PEER
   return check_launch();
 }
