@@ -71,6 +71,16 @@ def test_tc_paged_fp16_and_batch():
     _paged_case(8192, 32, 8, 16, dtype=torch.float16, batch=2, seed=5)
 
 
+def test_tc_config4_tree_shape():
+    # 128 nodes over 10 depths (config 4's tree): 512 rows per KV head, four CTAs
+    _paged_case(16384, 128, 13, 16, seed=7)
+
+
+def test_tc_config5_batch_of_96_node_trees():
+    # batch of 4 sequences with 96-node trees (config 5's per-sequence shape)
+    _paged_case(6144, 96, 12, 16, batch=4, seed=8)
+
+
 def test_tc_gqa_group_of_one():
     _paged_case(8192, 64, 8, 16, heads=8, kv_heads=8, seed=6)
 
