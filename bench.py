@@ -237,77 +237,84 @@ def run_ours(args, rank, world, dev):
         ms = float(t.item())
 
     # ---- end to end through the public API with host buffers -------------
+    # Every step copies its Q (and, on the tree rank, the keep mask) from
+    # pinned host memory, calls the public API, and copies O and the LSE back
+    # to pinned host memory; the step (copies included) is replayed as a CUDA
+    # graph like the device-timed steps, so Python overhead stays out.
     e2e = None
-    if world > 1 and not args.no_e2e:
-        # every rank: pinned host Q (and, on the tree rank, the keep mask) in,
-        # the merged output and LSE back to the host; slowest rank counts
+    if not args.no_e2e:
+        tree_rank = world == 1 or rank == world - 1
         q_host = [p.q.cpu().pin_memory() for p in probs]
         keep_host = [p.tree.keep.clone().pin_memory() for p in probs]
         out_host = [torch.empty(p.q.shape, dtype=p.q.dtype).pin_memory() for p in probs]
         lse_host = [torch.empty(p.q.shape[:3], dtype=torch.float32).pin_memory() for p in probs]
+        q_dev = torch.empty_like(p0.q)
+        keep_dev = torch.empty(p0.tree.keep.shape, dtype=p0.tree.keep.dtype, device=dev)
 
         def e2e_step(i):
             p = probs[i % rotate]
-            q = q_host[i % rotate].to(dev, non_blocking=True)
-            keep = keep_host[i % rotate].to(dev, non_blocking=True) if rank == world - 1 else None
-            o, lse = verifier(q, p.k_pool, p.v_pool, shard_len, keep, page_table=shards[i % rotate],
-                              return_lse=True)
+            q_dev.copy_(q_host[i % rotate], non_blocking=True)
+            if tree_rank:
+                keep_dev.copy_(keep_host[i % rotate], non_blocking=True)
+            if world == 1:
+                o, lse = verify_attention(q_dev, p.k_pool, p.v_pool, p.prefix_len, keep_dev, page_table=p.page_table,
+                                          return_lse=True)
+            else:
+                o, lse = verifier(q_dev, p.k_pool, p.v_pool, shard_len, keep_dev if tree_rank else None,
+                                  page_table=shards[i % rotate], return_lse=True)
             out_host[i % rotate].copy_(o, non_blocking=True)
             lse_host[i % rotate].copy_(lse, non_blocking=True)
 
         for i in range(args.warmup):
             e2e_step(i)
         torch.cuda.synchronize()
-        torch.distributed.barrier()
+        e2e_graphs = []
+        run_e2e = e2e_step
+        if not args.no_graph:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for i in range(rotate):
+                    e2e_step(i)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            for i in range(rotate):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    e2e_step(i)
+                e2e_graphs.append(g)
+            torch.cuda.synchronize()
+
+            def run_e2e(i):
+                e2e_graphs[i % rotate].replay()
+
+            for i in range(rotate):
+                run_e2e(i)
+            torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0 = time.perf_counter()
         e0.record()
         for i in range(args.steps):
-            e2e_step(i)
-        e1.record()
-        torch.cuda.synchronize()
-        wall = (time.perf_counter() - t0) * 1e3 / args.steps
-        t = torch.tensor([max(e0.elapsed_time(e1) / args.steps, wall)], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ems = float(t.item())
-        h2d = p0.q.numel() * p0.q.element_size() * world + p0.tree.keep.numel()
-        d2h = (p0.q.numel() * p0.q.element_size() + p0.q.shape[0] * p0.q.shape[1] * p0.q.shape[2] * 4) * world
-        e2e = {"value": round(alg_bytes / (ems * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ems, 4),
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "api": "specverify.runtime.sharded.SequenceShardedVerify (pinned host q/mask in, out/lse back "
-                      "to host on every rank)"}
-    if world == 1 and not args.no_e2e:
-        q_host = [p.q.cpu().pin_memory() for p in probs]
-        keep_host = [p.tree.keep.clone().pin_memory() for p in probs]
-        out_host = [torch.empty(p.q.shape, dtype=p.q.dtype).pin_memory() for p in probs]
-        lse_host = [torch.empty(p.q.shape[:3], dtype=torch.float32).pin_memory() for p in probs]
-
-        def e2e_step(i):
-            p = probs[i % rotate]
-            q = q_host[i % rotate].to(dev, non_blocking=True)
-            keep = keep_host[i % rotate].to(dev, non_blocking=True)
-            o, lse = verify_attention(q, p.k_pool, p.v_pool, p.prefix_len, keep, page_table=p.page_table,
-                                      return_lse=True)
-            out_host[i % rotate].copy_(o, non_blocking=True)
-            lse_host[i % rotate].copy_(lse, non_blocking=True)
-
-        for i in range(args.warmup):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0 = time.perf_counter()
-        e0.record()
-        for i in range(args.steps):
-            e2e_step(i)
+            run_e2e(i)
         e1.record()
         torch.cuda.synchronize()
         wall = (time.perf_counter() - t0) * 1e3 / args.steps
         ems = max(e0.elapsed_time(e1) / args.steps, wall)
-        h2d = p0.q.numel() * p0.q.element_size() + p0.tree.keep.numel()
-        d2h = p0.q.numel() * p0.q.element_size() + p0.q.shape[0] * p0.q.shape[1] * p0.q.shape[2] * 4
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e_graphs.clear()
+        h2d = p0.q.numel() * p0.q.element_size() * world + p0.tree.keep.numel() * p0.tree.keep.element_size()
+        d2h = (p0.q.numel() * p0.q.element_size() + p0.q.shape[0] * p0.q.shape[1] * p0.q.shape[2] * 4) * world
+        api = ("specverify.runtime.verify_attention" if world == 1 else
+               "specverify.runtime.sharded.SequenceShardedVerify")
         e2e = {"value": round(alg_bytes / (ems * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ems, 4),
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "api": "specverify.runtime.verify_attention (pinned host q/mask in, out/lse back to host)"}
+               "api": api + " (pinned host q/mask in, out/lse back to pinned host every step"
+                            + ("" if args.no_graph else "; the step replayed as a CUDA graph") + ")"}
 
     graphs.clear()   # graphs holding NCCL work are released before the process group goes
     total_bytes = alg_bytes  # whole job: the full 64K problem once per step (sharded or not)

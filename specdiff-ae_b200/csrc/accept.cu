@@ -308,8 +308,8 @@ int tv_accept(const tv_accept_args* a, void* stream) {
   const size_t smem = (size_t)rows * (sizeof(int64_t) + sizeof(int) + 2);
   if (smem > 200 * 1024) return TV_ERR_UNSUPPORTED;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(decide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return record_cuda_error(e);
+    const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(decide_kernel), (int)smem);
+    if (rc_smem != TV_OK) return rc_smem;
   }
   decide_kernel<<<1, S2_THREADS, smem, st>>>(rows, chunks, pv, pi, a->mode == 2 ? a->sampled : nullptr, a->draft,
                                              a->parent, a->pos, a->max_depth, a->next_tokens, a->result);

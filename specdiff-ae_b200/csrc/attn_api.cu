@@ -2,7 +2,10 @@
 // selection, and the log-sum-exp merge kernels.
 #include <string.h>
 
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "attn_epilogue.cuh"
 #include "attn_kernels.cuh"
@@ -17,6 +20,25 @@ extern "C" void tv_debug_set_trace(long long* device_buffer) { g_trace = device_
 int record_cuda_error(cudaError_t e) {
   g_last_cuda_error = cudaGetErrorString(e);
   return TV_ERR_LAUNCH;
+}
+
+int ensure_dynamic_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;   // (kernel, device) -> limit set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = done.find({kernel, dev});
+    if (it != done.end() && it->second >= bytes) return TV_OK;
+  }
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  std::lock_guard<std::mutex> lock(mu);
+  int& v = done[{kernel, dev}];
+  if (bytes > v) v = bytes;
+  return TV_OK;
 }
 
 namespace {

@@ -328,8 +328,8 @@ template <typename T, int D, bool PAGED, bool PRECISE>
 int launch_t(const AttnParams& p, cudaStream_t st) {
   constexpr int smem = Geo<D>::SMEM;
   auto kern = attn_mma_kernel<T, D, PAGED, PRECISE>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return record_cuda_error(e);
+  const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
+  if (rc_smem != TV_OK) return rc_smem;
   dim3 grid((p.R + BM - 1) / BM, p.B * p.Hkv, p.splits);
   kern<<<grid, NTHREADS, smem, st>>>(p);
   return check_launch();

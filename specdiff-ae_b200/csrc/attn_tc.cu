@@ -621,6 +621,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_wait_ld();
       if (edge) apply_keep(v, keep + 2);
       mx = fmaxf(mx, chunk_max(v));
+      // pass 2's first scores are loaded now; the latency hides behind the
+      // hand-off below
+      tmem_ld32(s_addr, v);
+      tmem_ld32(s_addr + 32, v + 32);
       // Reference after tile i-1 (published by the other warp of the quarter).
       float mprev = -INFINITY;
       if (i > 0) {
@@ -676,8 +680,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float mu = m_run == -INFINITY ? 0.f : m_run;
       // P: keys 0-63 into P-buffer columns 0-31, keys 64-127 into 32-63.
       uint32_t pk[32];
-      tmem_ld32(s_addr, v);
-      tmem_ld32(s_addr + 32, v + 32);
       tmem_wait_ld();
       if (edge) apply_keep(v, keep);
       l_run += chunk_exp<T>(v, sl2, mu, pk);
@@ -853,8 +855,8 @@ int launch_t(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, 
              cudaStream_t st) {
   using C = Cfg<PAIR>;
   auto kern = attn_tc_kernel<T, PAGED, PAIR>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (e != cudaSuccess) return record_cuda_error(e);
+  const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), C::SMEM);
+  if (rc_smem != TV_OK) return rc_smem;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tc_row_blocks(p.R), p.B * p.Hkv, p.splits);
   cfg.blockDim = dim3(THREADS, 1, 1);
@@ -867,7 +869,7 @@ int launch_t(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, p, mk, mv, box, tok_first);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, mk, mv, box, tok_first);
   if (e != cudaSuccess) return record_cuda_error(e);
   return check_launch();
 }

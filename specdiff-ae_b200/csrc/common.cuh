@@ -14,6 +14,9 @@ constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
 
 // Records the CUDA error text for tv_last_cuda_error() and maps it to a status.
 int record_cuda_error(cudaError_t e);
+// Raise a kernel's dynamic shared-memory limit to `bytes` on the current
+// device, once (the attribute call costs microseconds of host time).
+int ensure_dynamic_smem(const void* kernel, int bytes);
 
 inline int check_launch() {
   cudaError_t e = cudaGetLastError();

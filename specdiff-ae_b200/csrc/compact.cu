@@ -149,8 +149,7 @@ void dispatch_unit(int u, F&& f) {
 int set_smem(const void* fn, size_t bytes) {
   if (bytes <= 48 * 1024) return TV_OK;
   if (bytes > 227 * 1024) return TV_ERR_UNSUPPORTED;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  return e == cudaSuccess ? TV_OK : record_cuda_error(e);
+  return ensure_dynamic_smem(reinterpret_cast<const void*>(fn), (int)bytes);
 }
 
 }  // namespace
