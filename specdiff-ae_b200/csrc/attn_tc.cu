@@ -10,27 +10,29 @@
 // and the TMA work per SM halves.  A single CTA (cta_group::1) loads whole
 // tiles.
 //
-//   warp 0    TMA producer, all 32 lanes: lane j issues the boxes of page j
-//             (one box per page and 64-wide half of head_dim, straight from
-//             the paged pool through the page table; one box per half for a
-//             contiguous cache) into K and V rings of 128-byte-swizzled
-//             tiles.  Page ids are read a tile ahead.  Missing pages are
-//             fetched at an out-of-range page index, which TMA fills with
-//             zeros.  K and V have independent cursors.
+//   warps 0, 10  TMA producers, all 32 lanes: warp 0 loads K, warp 10 loads V,
+//             each with its own ring cursor.  A box is one chunk of 16 tokens
+//             (a page) times one 64-wide half of head_dim, read straight from
+//             the paged pool through the page table (page ids a tile ahead)
+//             into 128-byte-swizzled tiles; the boxes of a tile are spread
+//             over the lanes.  Missing pages are fetched at an out-of-range
+//             page index, which TMA fills with zeros.
 //   warps 11, 1  MMA issuers (one thread each, in the pair's first CTA):
 //             S = Q K^T (A = Q, B = K from shared memory, fp32 accumulator in
 //             TMEM) and O += P V (A = P read from TMEM, B = V from shared
 //             memory), each issued as soon as its inputs are ready.
-//   warps 2-9 softmax: two warps per TMEM lane quarter; each thread owns one
-//             query row (one TMEM lane) and 64 of the tile's 128 key columns.
-//             The two warps exchange row maxima through shared memory; the
-//             bitmask applies on the tail tiles only; the running max only
-//             moves when it grows by more than 2^8, so O is rescaled rarely.
-//             P (16-bit pairs) is written over the scores.
+//   warps 2-9 softmax: warps 2-5 take the even tiles, warps 6-9 the odd ones;
+//             warp w covers TMEM lane quarter w % 4, and each thread owns one
+//             query row and all 128 keys of its tiles.  The running reference
+//             max passes from tile to tile through shared memory; it only
+//             moves when a tile's max exceeds it by more than 2^8, so O is
+//             rescaled rarely.  The bitmask applies on the tail tiles only.
 //
-// S is triple-buffered in TMEM (S0 S1 S2 O, 128 columns each): S(j) reuses
-// the buffer of P(j-3) once PV(j-3) retired, so S runs ahead of the softmax
-// and the softmax warps never wait on their own PV.
+// Tensor memory (512 columns): S0 S1 (fp32 scores, 128 columns each), P0 P1
+// (16-bit pairs, 64 columns each), O (128 columns).  S(j) reuses its buffer
+// once the softmax warps have read S(j-2); P(i) reuses its buffer once
+// PV(i-2) has retired, so a softmax warp never waits for the PV of the tile
+// it just finished.
 //
 // Every mbarrier wait is bounded (2 s); on expiry the CTA raises an abort
 // flag (in both CTAs of a pair), records a status word, poisons its rows with
@@ -481,8 +483,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1 || warp == 11) {
     // ---------------------------------------------------------------- MMA issuers
     // Two threads (of the pair's first CTA) feed the tensor pipe: warp 11
-    // issues S(j) = Q K^T as soon as K(j) has landed and the PV that last
-    // read its buffer (PV(j-3)) has retired; warp 1 issues O += P(i) V(i) as
+    // issues S(j) = Q K^T as soon as K(j) has landed and the softmax warps
+    // have read S(j-2) out of its buffer; warp 1 issues O += P(i) V(i) as
     // soon as P(i) and V(i) are ready.  Each keeps the pipe busy while the
     // other waits.
     if (lane == 0 && rank == 0 && NT > 0) {
@@ -566,7 +568,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp >= 2 && warp < 10) {
     // ---------------------------------------------------------------- softmax
     // Warps 2-5 take the even tiles, warps 6-9 the odd tiles (tile i in S
-    // buffer i % 3), so the two warps sharing a scheduler (and its MUFU unit)
+    // buffer i % 2), so the two warps sharing a scheduler (and its MUFU unit)
     // work on successive tiles at the same time.  Warp w covers TMEM lane quarter w % 4: each
     // thread owns one query row and all 128 keys of its tiles.  The running
     // reference max passes from tile to tile through shared memory (one
@@ -597,7 +599,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      if (lane == 0 && warp == 2) TV_TRACE(4, i);
+      if (lane == 0 && (warp == 2 || warp == 6)) TV_TRACE(4, i);
       const uint32_t s_addr = lane_base + (uint32_t)((i % SBUF) * BN);
       const int n0 = (t0 + i) * BN;
       // Tiles wholly inside the prefix take the unmasked path; the bitmask is
@@ -649,6 +651,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bars->mref[rr] = m_run;       // reference for tile i+1
       __syncwarp();
       if (lane == 0) mbar_arrive(ref_bar);
+      if (lane == 0 && (warp == 2 || warp == 6)) TV_TRACE(5, i);
       const bool need_o = bump && i > 0;
       if (__any_sync(0xffffffffu, need_o)) {
         // O holds tiles up to i-1 scaled to mprev; PV(i-1) must retire first.
@@ -689,6 +692,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // All of S(i) is in registers: its buffer can take S(i + SBUF).
       tc_fence_before();
       __syncwarp();
+      if (lane == 0 && (warp == 2 || warp == 6)) TV_TRACE(15, i);
       if (lane == 0) {
         if (PAIR) mbar_arrive_cluster(mapa_shared(&bars->s_free[i % SBUF], 0));
         else mbar_arrive(&bars->s_free[i % SBUF]);
