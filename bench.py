@@ -2,7 +2,7 @@
 """Benchmark: tree-verify attention on B200 (BASELINE config 2 and the sharded scaling run).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|config2|sharded]
+                    [--workload verify|rope-append]
 
 A step is one verify-attention pass of one layer over the config-2 problem:
 64K-token paged KV cache (16-token pages, seeded random page permutation),
@@ -25,6 +25,13 @@ the host inside the timed region; the KV cache is device-resident state.
 --impl reference times the reference's own CPU path (prefix attention + tree
 attention + merge on repeat_kv-expanded K/V, fp32, restated in oracle/) on the
 host cores over a bounded sample of the same problem.
+
+--workload rope-append (one GPU) measures the step before verify attention
+instead: rotary embedding of q and k plus the append of the rotated k and v
+to the KV cache (``tv_rope_append``), for a batch of 16 sequences x 2048 new
+tokens (Llama-3.1-8B heads, bf16), next to the reference's own sequence of
+torch ops for the same step on the same GPU; ``verify_shape_us`` is the
+65-row verify step (B = 1).
 """
 
 from __future__ import annotations
@@ -423,6 +430,127 @@ def run_reference(args, rank, world):
 _JSON_OUT = sys.stdout
 
 
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum) of one tv_rope_append
+# launch on the rope-append workload below.
+NCU_ROPE_TRAFFIC_BYTES = 762_554_624
+
+
+def _graph_us(fn, reps: int, steps: int, warmup: int) -> float:
+    """Device time per call of `fn`, replayed as a CUDA graph of `reps` calls."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (steps * reps)
+    del g
+    return us
+
+
+def run_rope(args):
+    """Rotary embedding + KV append (the step before verify attention)."""
+    from specverify.runtime import KVCache, rope_append
+    from oracle import rope as orope
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --workload rope-append needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    h, hkv, d, start = 32, 8, 128, 8192
+
+    def problem(b, t):
+        # q / k / v as views of the projection outputs, as LlamaAttention holds them
+        q = torch.randn(b, t, h * d, generator=g).bfloat16().to(dev).view(b, t, h, d).transpose(1, 2)
+        kv = torch.randn(b, t, 2 * hkv * d, generator=g).bfloat16().to(dev)
+        k = kv[..., :hkv * d].reshape(b, t, hkv, d).transpose(1, 2)
+        v = kv[..., hkv * d:].reshape(b, t, hkv, d).transpose(1, 2)
+        cos_t, sin_t = orope.rope_table(d, start + t, 500000.0)
+        cos = torch.from_numpy(cos_t).bfloat16().to(dev)[None, None]
+        sin = torch.from_numpy(sin_t).bfloat16().to(dev)[None, None]
+        pos = (start - 1 + torch.arange(t) // 8).view(1, t).expand(b, t).contiguous().to(dev)
+        kd = torch.zeros(b, hkv, start + t, d, dtype=torch.bfloat16, device=dev)
+        vd = torch.zeros_like(kd)
+        kc, vc = KVCache(kd, torch.tensor(start)), KVCache(vd, torch.tensor(start))
+        qo = torch.empty(b, h, t, d, dtype=torch.bfloat16, device=dev)
+
+        def ours():
+            kc.current_length.fill_(start)
+            vc.current_length.fill_(start)
+            rope_append(q, k, v, cos, sin, pos, kc, vc, out=qo, validate=False)
+
+        def rot(x):
+            return torch.cat((-x[..., d // 2:], x[..., :d // 2]), dim=-1)
+
+        def reference_ops():      # llama_target_model.py:443-449 and cache_state.py:63-64
+            c = cos.squeeze(1).squeeze(0)[pos].unsqueeze(1)
+            s_ = sin.squeeze(1).squeeze(0)[pos].unsqueeze(1)
+            qe = q * c + rot(q) * s_
+            ke = k * c + rot(k) * s_
+            kd.narrow(2, start, t).copy_(ke)
+            vd.narrow(2, start, t).copy_(v)
+            return qe
+
+        alg = 2 * q.numel() * 2 + 2 * k.numel() * 2 + 2 * v.numel() * 2 + 2 * b * t * d * 2
+        return ours, reference_ops, alg, (q, k, v, cos, sin, pos)
+
+    b, t = 16, 2048
+    ours, ref_ops, alg, _ = problem(b, t)
+    us = _graph_us(ours, 4, args.steps, args.warmup)
+    ref_us = _graph_us(ref_ops, 4, max(3, args.steps // 4), args.warmup)
+    small, small_ref, _, small_in = problem(1, 65)
+    small_us = _graph_us(small, 20, args.steps, args.warmup)
+    small_ref_us = _graph_us(small_ref, 20, args.steps, args.warmup)
+    peak, kind = peaks()
+    gbs = alg / (us * 1e-6) / 1e9
+    res = {
+        "metric": "rope + KV append GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v)",
+        "config": {"workload": f"rope-append: B={b} x {t} new tokens, 32/8 heads, head_dim 128, contiguous cache at "
+                               f"{start}", "launch": "CUDA graph replays of the public API call",
+                   "l2": "inputs larger than L2 (822 MB moved per call)", "algorithmic_bytes_per_step": alg},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "traffic": NCU_ROPE_TRAFFIC_BYTES,
+                     "peak_kind": kind, "kernel": "rope_append_kernel (one launch per call)"},
+        "gpu_launches": args.steps * 4,
+        "reference_ops_on_gpu": {"us": round(ref_us, 2), "speedup": round(ref_us / us, 2),
+                                 "what": "the reference's torch ops for the step (cos/sin gather, q*cos + "
+                                         "rotate_half(q)*sin for q and k, two KVCache.cat copies)"},
+        "verify_shape_us": {"ours": round(small_us, 2), "reference_ops": round(small_ref_us, 2),
+                            "config": "B=1, 65 rows, 32/8 heads, head_dim 128"},
+    }
+    if not args.no_cpu_baseline:
+        q, k, v, cos, sin, pos = small_in
+        qf, kf = q.float().cpu().numpy(), k.float().cpu().numpy()
+        cf, sf = cos[0, 0].float().cpu().numpy(), sin[0, 0].float().cpu().numpy()
+        pf = pos.cpu().numpy()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 2.0:
+            orope.apply_rotary_pos_emb(qf, kf, cf, sf, pf, "bf16")
+            n += 1
+        sec = (time.perf_counter() - t0) / n
+        small_alg = 2 * q.numel() * 2 + 2 * k.numel() * 2 + 2 * v.numel() * 2 + 2 * 65 * d * 2
+        res["cpu_baseline"] = {"value": round(small_alg / sec / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                               "sample": f"numpy restatement, B=1 x 65 rows; {sec * 1e6:.0f} us per call"}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -432,6 +560,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
+    ap.add_argument("--workload", choices=["verify", "rope-append"], default="verify")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -445,6 +574,10 @@ def main():
     _JSON_OUT = os.fdopen(os.dup(1), "w")
     sys.stdout.flush()
     os.dup2(2, 1)
+    if args.workload == "rope-append":
+        if rank == 0:
+            print(json.dumps(run_rope(args)), file=_JSON_OUT, flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:

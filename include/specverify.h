@@ -288,6 +288,63 @@ int tv_arena_gather(int32_t layers, int32_t heads, const uint64_t* src_k, const 
 int tv_gather_page_table(const int32_t* page_table, int32_t table_len, const int32_t* chunk_ids,
                          int32_t nchunks, int32_t pages_per_chunk, int32_t* out, void* stream);
 
+/* ---- rotary embedding + KV append -------------------------------------------
+ * Replaces the step before the verify attention in LlamaAttention.forward
+ * (llama_target_model.py:765-783): rotate_half RoPE of q and k
+ * (apply_rotary_pos_emb :429-449, apply_rotary_pos_emb_L31 :452-474) and
+ * KVCache.cat of the rotated k and of v (cache_state.py:52-66), one launch.
+ *
+ * Tensors are [B, heads, T, D] with any strides (element units) and unit
+ * stride on D; D even, D <= 256.  dtype covers q, k, v, cos, sin, the outputs
+ * and the caches.  Output element (b, h, t, d) of q (and k):
+ *   R(R(x[d] * cos[d]) + R(rot(x)[d] * sin[d])),  rot(x) = cat(-x2, x1),
+ * R = rounding to dtype after every product and the sum, as the reference's
+ * torch element-wise ops do (fp32: no fused multiply-add).  cos / sin element
+ * (b, t, d) is read at cos[b * cs_sb + row * cs_sr + d] with row =
+ * pos[b * pos_sb + t] when pos is given (the cached table gathered by
+ * position ids) or row = t (per-token tables, as LlamaRotaryEmbedding_L31
+ * returns them).  q_out may alias q.  k_out (optional) receives rotated k.
+ * Cache append (optional, k_cache / v_cache): token t of batch b goes to
+ * token index start + t of the cache:
+ *   page_table == NULL: contiguous [B, kv_heads, capacity, D] with strides
+ *     (kc_sb, kc_sh, kc_st) / (vc_sb, vc_sh, vc_st);
+ *   page_table != NULL: paged pool [num_pages, kv_heads, page_size, D], page
+ *     id page_table[b * pt_sb + idx / page_size], strides (kc_sb = page,
+ *     kc_sh = head, kc_st = token) and the same for v.
+ * A position row outside [0, cs_rows), a token index past capacity or a page
+ * id outside [0, num_pages) skips that token and sets *status (if given) to
+ * TV_ERR_INPUT. */
+typedef struct tv_rope_args {
+  int32_t dtype;                  /* TV_BF16, TV_F16 or TV_F32              */
+  int32_t batch, tokens, heads, kv_heads, head_dim;
+  const void* q;
+  int64_t q_sb, q_sh, q_st;
+  const void* k;
+  int64_t k_sb, k_sh, k_st;
+  const void* v;                  /* may be NULL when nothing is appended    */
+  int64_t v_sb, v_sh, v_st;
+  const void* cos;
+  const void* sin;
+  int64_t cs_sb, cs_sr, cs_rows;
+  const int64_t* pos;             /* NULL: row = t                           */
+  int64_t pos_sb;
+  void* q_out;                    /* required                                */
+  int64_t qo_sb, qo_sh, qo_st;
+  void* k_out;                    /* NULL: rotated k only goes to the cache  */
+  int64_t ko_sb, ko_sh, ko_st;
+  void* k_cache;                  /* NULL: no append                         */
+  int64_t kc_sb, kc_sh, kc_st;
+  void* v_cache;
+  int64_t vc_sb, vc_sh, vc_st;
+  int64_t start, capacity;
+  const int32_t* page_table;
+  int64_t pt_sb;
+  int32_t page_size, num_pages;
+  int32_t* status;                /* optional device word                    */
+} tv_rope_args;
+
+int tv_rope_append(const tv_rope_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,4 +20,6 @@ acceptance  greedy and sample-and-match acceptance, path trace, contiguous
 paged       page-table copy-on-write bookkeeping and paged compaction
 arena       chunk-arena differential update
 bundles     branching-ancestor bundle grouping
+rope        rotary embedding of q / k and the KV-cache append (numpy, bit-exact
+            emulation of the reference's bf16 / fp16 / fp32 element-wise ops)
 """

@@ -66,6 +66,26 @@ class AcceptArgs(ctypes.Structure):
     ]
 
 
+class RopeArgs(ctypes.Structure):
+    """Mirror of ``tv_rope_args``."""
+    _fields_ = [
+        ("dtype", c_i32), ("batch", c_i32), ("tokens", c_i32), ("heads", c_i32), ("kv_heads", c_i32),
+        ("head_dim", c_i32),
+        ("q", c_vp), ("q_sb", c_i64), ("q_sh", c_i64), ("q_st", c_i64),
+        ("k", c_vp), ("k_sb", c_i64), ("k_sh", c_i64), ("k_st", c_i64),
+        ("v", c_vp), ("v_sb", c_i64), ("v_sh", c_i64), ("v_st", c_i64),
+        ("cos", c_vp), ("sin", c_vp), ("cs_sb", c_i64), ("cs_sr", c_i64), ("cs_rows", c_i64),
+        ("pos", c_vp), ("pos_sb", c_i64),
+        ("q_out", c_vp), ("qo_sb", c_i64), ("qo_sh", c_i64), ("qo_st", c_i64),
+        ("k_out", c_vp), ("ko_sb", c_i64), ("ko_sh", c_i64), ("ko_st", c_i64),
+        ("k_cache", c_vp), ("kc_sb", c_i64), ("kc_sh", c_i64), ("kc_st", c_i64),
+        ("v_cache", c_vp), ("vc_sb", c_i64), ("vc_sh", c_i64), ("vc_st", c_i64),
+        ("start", c_i64), ("capacity", c_i64),
+        ("page_table", c_vp), ("pt_sb", c_i64), ("page_size", c_i32), ("num_pages", c_i32),
+        ("status", c_vp),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "tv_status_string": (ctypes.c_char_p, [c_i32]),
@@ -87,6 +107,7 @@ _SIGNATURES = {
     "tv_arena_gather": (c_i32, [c_i32, c_i32, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, c_i64, c_i64, c_i64, c_i32,
                                 c_i32, c_i32, c_vp, c_i32, c_vp]),
     "tv_gather_page_table": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_i32, c_vp, c_vp]),
+    "tv_rope_append": (c_i32, [ctypes.POINTER(RopeArgs), c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

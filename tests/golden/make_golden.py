@@ -32,6 +32,11 @@ bundles.json
     ``BundleScheduler.schedule_bundles`` on seeded trees.
 bundle_verify.npz
     ``FusedBundleVerifier`` torch path.
+rope_bf16.npz / rope_f16.npz / rope_f32.npz
+    ``LlamaRotaryEmbedding`` (theta 500000) cached cos/sin tables,
+    ``apply_rotary_pos_emb`` with tree position ids, ``apply_rotary_pos_emb_L31``
+    on the gathered per-token tables, and ``KVCache.cat`` of the rotated k and
+    of v into a pre-filled cache at ``current_length``.
 """
 
 from __future__ import annotations
@@ -349,19 +354,74 @@ def gen_bundle_verify(bv, path: Path):
                         out=o.numpy(), lse=lse.numpy(), stats=json.dumps(ver.get_statistics()))
 
 
+def _enc16(t: torch.Tensor) -> np.ndarray:
+    """bf16 as uint16 bit patterns, fp16 / fp32 as numpy arrays."""
+    if t.dtype == torch.bfloat16:
+        return _bf16_bits(t)
+    return t.contiguous().numpy()
+
+
+def gen_rope(ltm, dtype, path: Path):
+    from diffspec.runtime import cache_state as cs                # noqa: E402
+    gen = torch.Generator().manual_seed(4321)
+    b, h, hkv, t, d, max_pos, prefix, budget = 2, 8, 2, 17, 64, 512, 300, 64
+    # the module builds its cache in the default dtype and casts on use (:152-211)
+    rot = ltm.LlamaRotaryEmbedding(d, max_position_embeddings=max_pos, base=500000)
+    q = torch.randn(b, h, t, d, generator=gen).to(dtype)
+    k = torch.randn(b, hkv, t, d, generator=gen).to(dtype)
+    v = torch.randn(b, hkv, t, d, generator=gen).to(dtype)
+    depth = torch.arange(t) // 3                                   # tree-like: several tokens per depth
+    position_ids = torch.stack([prefix + depth, prefix + 7 + depth])   # [B, T]
+    cos, sin = rot(v, seq_len=max_pos)                             # [1, 1, max_pos, D] in dtype
+    q_embed, k_embed = ltm.apply_rotary_pos_emb(q, k, cos, sin, position_ids)
+    cos_tok = cos.squeeze(1).squeeze(0)[position_ids]              # [B, T, D]
+    sin_tok = sin.squeeze(1).squeeze(0)[position_ids]
+    q_l31, k_l31 = ltm.apply_rotary_pos_emb_L31(q, k, cos_tok, sin_tok)
+    kdata = torch.randn(b, hkv, budget, d, generator=gen).to(dtype)
+    vdata = torch.randn(b, hkv, budget, d, generator=gen).to(dtype)
+    k_before, v_before = kdata.clone(), vdata.clone()
+    start = 40                                                     # cache index (positions are separate)
+    kc = cs.KVCache(kdata, torch.tensor(start, dtype=torch.long))
+    vc = cs.KVCache(vdata, torch.tensor(start, dtype=torch.long))
+    k_states = kc.cat(k_embed, dim=2)
+    v_states = vc.cat(v, dim=2)
+    np.savez_compressed(
+        path, dtype=str(dtype), position_ids=position_ids.numpy(), start=start,
+        q=_enc16(q), k=_enc16(k), v=_enc16(v),
+        cos=_enc16(cos.squeeze(1).squeeze(0)), sin=_enc16(sin.squeeze(1).squeeze(0)),
+        q_embed=_enc16(q_embed), k_embed=_enc16(k_embed), q_l31=_enc16(q_l31), k_l31=_enc16(k_l31),
+        k_cache_before=_enc16(k_before), v_cache_before=_enc16(v_before),
+        k_cache_after=_enc16(kdata), v_cache_after=_enc16(vdata),
+        k_states_len=k_states.shape[2], v_states_len=v_states.shape[2])
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DIFFSPEC_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default="", help="comma-separated subset: attention, accept, paged, arena, "
+                                               "bundles, bundle_verify, rope")
     args = ap.parse_args()
+    only = set(filter(None, args.only.split(",")))
+    want = (lambda name: not only or name in only)
     torch.manual_seed(0)
     ta, ltm, tv, pkv, ca, bs, bv = _import_reference(args.reference)
-    gen_attention(ta, ltm, torch.float32, HERE / "attn_fp32.npz")
-    gen_attention(ta, ltm, torch.bfloat16, HERE / "attn_bf16.npz")
-    gen_accept(tv, HERE / "accept_greedy.npz", HERE / "accept_sample.npz")
-    gen_paged(pkv, HERE / "paged.npz")
-    gen_arena(ca, HERE / "arena.npz")
-    gen_bundles(bs, HERE / "bundles.json")
-    gen_bundle_verify(bv, HERE / "bundle_verify.npz")
+    if want("attention"):
+        gen_attention(ta, ltm, torch.float32, HERE / "attn_fp32.npz")
+        gen_attention(ta, ltm, torch.bfloat16, HERE / "attn_bf16.npz")
+    if want("accept"):
+        gen_accept(tv, HERE / "accept_greedy.npz", HERE / "accept_sample.npz")
+    if want("paged"):
+        gen_paged(pkv, HERE / "paged.npz")
+    if want("arena"):
+        gen_arena(ca, HERE / "arena.npz")
+    if want("bundles"):
+        gen_bundles(bs, HERE / "bundles.json")
+    if want("bundle_verify"):
+        gen_bundle_verify(bv, HERE / "bundle_verify.npz")
+    if want("rope"):
+        gen_rope(ltm, torch.bfloat16, HERE / "rope_bf16.npz")
+        gen_rope(ltm, torch.float16, HERE / "rope_f16.npz")
+        gen_rope(ltm, torch.float32, HERE / "rope_f32.npz")
     print("golden fixtures written to", HERE)
 
 

@@ -52,3 +52,35 @@ def test_host_only_calls(lib):
     # shape / null validation happens on the host, before any device work
     lib.tv_attn_workspace_size.restype = ctypes.c_int32
     assert lib.tv_attn_workspace_size(None, None) != 0
+
+
+def test_ctypes_structs_match_the_header(tmp_path):
+    """The ctypes mirrors have the C structs' size and every field offset
+    (compiled against include/specverify.h with the host C compiler)."""
+    import shutil
+    import subprocess
+    import sys
+    if shutil.which("gcc") is None:
+        pytest.skip("no host C compiler")
+    sys.path.insert(0, str(ROOT / "specdiff-ae_b200"))
+    from specverify import _lib
+    mirrors = {"tv_attn_args": _lib.AttnArgs, "tv_accept_args": _lib.AcceptArgs, "tv_rope_args": _lib.RopeArgs}
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "specverify.h"', "int main(void) {"]
+    for cname, py in mirrors.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {}
+    for line in filter(None, out):
+        cname, field, value = line.split()
+        got[(cname, field)] = int(value)
+    for cname, py in mirrors.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, f"{cname}.{fname}"

@@ -13,10 +13,11 @@ from __future__ import annotations
 import json
 
 import numpy as np
+import pytest
 import torch
 
 from conftest import bf16_from_bits, load_golden
-from oracle import acceptance, arena, attention, bundles, paged
+from oracle import acceptance, arena, attention, bundles, paged, rope
 
 
 def _t(x, dtype):
@@ -188,3 +189,57 @@ def test_lse_merge_equals_full_softmax():
     o, l = attention.lse_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]))
     assert torch.allclose(o, full, atol=1e-5)
     assert torch.allclose(l, full_lse, atol=1e-5)
+
+
+def _rope_decode(z, key):
+    """Fixture array -> (float32 values, kind)."""
+    kind = {"torch.bfloat16": "bf16", "torch.float16": "f16", "torch.float32": "f32"}[str(z["dtype"])]
+    a = z[key]
+    return (bf16_from_bits(a) if kind == "bf16" else np.asarray(a, dtype=np.float32)), kind
+
+
+@pytest.mark.parametrize("name", ["rope_bf16.npz", "rope_f16.npz", "rope_f32.npz"])
+def test_rope_oracle_matches_reference(name):
+    z = load_golden(name)
+    q, kind = _rope_decode(z, "q")
+    k, _ = _rope_decode(z, "k")
+    v, _ = _rope_decode(z, "v")
+    cos, _ = _rope_decode(z, "cos")
+    sin, _ = _rope_decode(z, "sin")
+    pos = z["position_ids"]
+    qe, ke = rope.apply_rotary_pos_emb(q, k, cos, sin, pos, kind)
+    # bit-identical: compare the float32 carriers exactly (all values are
+    # representable in the element type)
+    np.testing.assert_array_equal(qe, _rope_decode(z, "q_embed")[0])
+    np.testing.assert_array_equal(ke, _rope_decode(z, "k_embed")[0])
+    q31, k31 = rope.apply_rotary_pos_emb_l31(q, k, cos[pos], sin[pos], kind)
+    np.testing.assert_array_equal(q31, _rope_decode(z, "q_l31")[0])
+    np.testing.assert_array_equal(k31, _rope_decode(z, "k_l31")[0])
+    start = int(z["start"])
+    kc, klen = rope.kv_cat(_rope_decode(z, "k_cache_before")[0], start, ke)
+    vc, vlen = rope.kv_cat(_rope_decode(z, "v_cache_before")[0], start, v)
+    np.testing.assert_array_equal(kc, _rope_decode(z, "k_cache_after")[0])
+    np.testing.assert_array_equal(vc, _rope_decode(z, "v_cache_after")[0])
+    assert klen == int(z["k_states_len"]) and vlen == int(z["v_states_len"])
+
+
+def test_rope_rounding_helpers():
+    x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.4e38, np.inf], dtype=np.float32)
+    b = rope.f32_to_bf16_bits(x)
+    # 1 + 2^-8 is a tie between 1 and 1 + 2^-7: nearest-even gives 1
+    assert b[1] == rope.f32_to_bf16_bits(np.float32(1.0))
+    np.testing.assert_array_equal(rope.bf16_bits_to_f32(b)[[0, 3, 5]], x[[0, 3, 5]])
+    assert np.isinf(rope.bf16_bits_to_f32(b)[4])      # rounds past the largest bf16
+    assert np.isnan(rope.round_to(np.float32(np.nan), "bf16"))
+
+
+def test_rope_table_matches_reference_cast():
+    """The reference's cached tables are float32 cos/sin cast to the element
+    type; the restated table agrees with the fixture's bf16 table except where
+    float32 cos/sin of the same argument round differently (last-ulp libm
+    differences land on a bf16 rounding boundary very rarely)."""
+    z = load_golden("rope_bf16.npz")
+    cos, sin = rope.rope_table(z["cos"].shape[1], z["cos"].shape[0], 500000.0)
+    got = rope.round_to(cos, "bf16")
+    ref = bf16_from_bits(z["cos"])
+    assert np.mean(got == ref) > 0.999
