@@ -433,6 +433,8 @@ _JSON_OUT = sys.stdout
 # ncu (dram__bytes_read.sum + dram__bytes_write.sum) of one tv_rope_append
 # launch on the rope-append workload below.
 NCU_ROPE_TRAFFIC_BYTES = 762_554_624
+# the same for one lmhead_scan_kernel launch on the lmhead-accept workload
+NCU_LMHEAD_TRAFFIC_BYTES = 1_056_964_720
 
 
 def _graph_us(fn, reps: int, steps: int, warmup: int) -> float:
@@ -551,6 +553,73 @@ def run_rope(args):
     return res
 
 
+def run_lmhead(args):
+    """lm_head + acceptance in one pass (the step after verify attention)."""
+    from specverify.draft.tree_verification import accept, accept_from_hidden
+    from oracle import acceptance as oacc
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --workload lmhead-accept needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    rows, hidden, vocab, max_depth = 65, 4096, 128256, 8
+    x = torch.randn(rows, hidden, generator=g).bfloat16().to(dev)
+    w = (0.02 * torch.randn(vocab, hidden, generator=g)).bfloat16().to(dev)
+    depth = torch.cat([torch.zeros(1, dtype=torch.long), 1 + torch.arange(rows - 1) // 8])
+    parent = torch.cat([torch.full((8,), -1), torch.arange(rows - 9) // 8 * 8]).to(dev)
+    pos = (65535 + depth).to(dev)
+    draft = torch.randint(0, vocab, (rows,), generator=g).to(dev)
+
+    def ours():
+        accept_from_hidden(x, w, draft, parent, pos, max_depth)
+
+    def reference_ops():     # diffspec_model.py:229-231 then tree_verification.py:102
+        return torch.argmax(torch.nn.functional.linear(x, w), dim=-1)
+
+    def unfused_ours():
+        accept(torch.nn.functional.linear(x, w), draft, parent, pos, max_depth)
+
+    us = _graph_us(ours, 5, args.steps, args.warmup)
+    ref_us = _graph_us(reference_ops, 5, args.steps, args.warmup)
+    unf_us = _graph_us(unfused_ours, 5, args.steps, args.warmup)
+    alg = vocab * hidden * 2 + rows * hidden * 2 + 2 * rows * 8
+    peak, kind = peaks()
+    gbs = alg / (us * 1e-6) / 1e9
+    res = {
+        "metric": "lm_head + acceptance GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) hidden, "
+                                                                          "N(0,0.02) weight)",
+        "config": {"workload": f"lmhead-accept: {rows} rows x hidden {hidden} x vocab {vocab} (Llama-3.1-8B "
+                               f"lm_head), greedy, 64-node depth-8 tree",
+                   "launch": "CUDA graph replays of the public API call",
+                   "l2": "weight (1.05 GB) larger than L2", "algorithmic_bytes_per_step": alg,
+                   "flops_per_step": 2 * 128 * hidden * vocab},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "traffic": NCU_LMHEAD_TRAFFIC_BYTES, "peak_kind": kind,
+                     "kernel": "lmhead_scan_kernel + acceptance (two launches per call); traffic is "
+                               "lmhead_scan_kernel's per launch (ncu)"},
+        "gpu_launches": args.steps * 5 * 3,
+        "reference_ops_on_gpu": {"us": round(ref_us, 2), "speedup": round(ref_us / us, 3),
+                                 "what": "the reference's ops: lm_head (torch linear, cuBLAS) writing bf16 logits "
+                                         "[65, 128256], then torch.argmax per node"},
+        "unfused_ours_us": round(unf_us, 2),
+    }
+    if not args.no_cpu_baseline:
+        xs, ws = x.float().cpu().numpy(), w[:8192].float().cpu().numpy()
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 2.0:
+            oacc.argmax_rows(xs @ ws.T)
+            n += 1
+        sec = (time.perf_counter() - t0) / n
+        res["cpu_baseline"] = {"value": round(ws.size * 2 / sec / 1e9, 3), "unit": "GB/s",
+                               "cores": torch.get_num_threads(), "kind": "port",
+                               "sample": f"numpy lm_head + argmax over the first 8192 vocab rows; "
+                                         f"{sec * 1e3:.1f} ms per call"}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -560,7 +629,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
-    ap.add_argument("--workload", choices=["verify", "rope-append"], default="verify")
+    ap.add_argument("--workload", choices=["verify", "rope-append", "lmhead-accept"], default="verify")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -577,6 +646,10 @@ def main():
     if args.workload == "rope-append":
         if rank == 0:
             print(json.dumps(run_rope(args)), file=_JSON_OUT, flush=True)
+        return
+    if args.workload == "lmhead-accept":
+        if rank == 0:
+            print(json.dumps(run_lmhead(args)), file=_JSON_OUT, flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, rank, world)

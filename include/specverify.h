@@ -345,6 +345,45 @@ typedef struct tv_rope_args {
 
 int tv_rope_append(const tv_rope_args* args, void* stream);
 
+/* ---- lm_head + acceptance ----------------------------------------------------
+ * Replaces the step after the verify attention: logits = lm_head(hidden)
+ * (diffspec_model.py:229-231, a [rows, vocab] tensor) followed by the argmax
+ * or sampling of verify_new (tree_verification.py:100-162).  One tensor-core
+ * GEMM streams the weight once and reduces every row's logits in its
+ * epilogue, so the logits are never written; then the acceptance rule of
+ * tv_accept runs on the per-row picks.
+ *   x [rows, hidden] (row stride x_sm), weight [vocab, hidden] (row stride
+ *   w_sv), dtype TV_BF16 or TV_F16 for both; rows <= 128; hidden a
+ *   multiple of 64; 16-byte aligned rows.
+ * Each logit is the fp32 dot product rounded to dtype (the reference's lm_head
+ * returns dtype logits); mode 0 takes the argmax (ties: smaller index, a NaN
+ * beats every number), mode 1 the argmax of logit / temperature + Gumbel noise
+ * (the same noise as tv_accept mode 1 for the same seed / offset).
+ * draft / parent / pos / max_depth / result as tv_accept; draft == NULL
+ * computes next_tokens only.  workspace: tv_lmhead_accept_workspace_size. */
+typedef struct tv_lmhead_args {
+  int32_t dtype;
+  int32_t rows, hidden, vocab;
+  const void* x;
+  int64_t x_sm;
+  const void* weight;
+  int64_t w_sv;
+  int32_t mode;
+  float temperature;
+  uint64_t seed, offset;
+  const int64_t* draft;
+  const int64_t* parent;
+  const int64_t* pos;
+  int32_t max_depth;
+  int64_t* next_tokens;
+  int64_t* result;
+  void* workspace;
+  size_t workspace_bytes;
+} tv_lmhead_args;
+
+int tv_lmhead_accept_workspace_size(const tv_lmhead_args* args, size_t* bytes);
+int tv_lmhead_accept(const tv_lmhead_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,55 +13,16 @@
 // ancestor closure, the first-maximum pick of the deepest accepted node, and
 // the root-to-node path.  The reference copies parents, drafts and tokens to
 // the host for this (tree_verification.py:112-118).
-#include "common.cuh"
+#include "accept_common.cuh"
 
 namespace tv {
 namespace {
 
+using namespace acc;
+
 constexpr int S1_THREADS = 256;
 constexpr int S2_THREADS = 512;
 constexpr int kMaxChunks = 64;
-
-struct Best {
-  float v;
-  int i;
-};
-
-__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
-  const bool n1 = v1 != v1, n2 = v2 != v2;
-  if (n1 || n2) return n1 && (!n2 || i1 < i2);
-  return v1 > v2 || (v1 == v2 && i1 < i2);
-}
-
-__device__ __forceinline__ void take(Best& b, float v, int i) {
-  if (better(v, i, b.v, b.i)) { b.v = v; b.i = i; }
-}
-
-// Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as
-// easy as 1, 2, 3", SC'11): 10 rounds of two 32x32->64 multiplies with
-// Weyl-sequence key bumps.
-__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
-  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
-#pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    const uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
-    const uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
-    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
-    k.x += W0;
-    k.y += W1;
-  }
-  return c;
-}
-
-// Gumbel(0, 1) noise for (row, token j) from a 24-bit uniform in (0, 1).
-__device__ __forceinline__ float gumbel(uint64_t seed, uint64_t offset, int row, int j) {
-  const uint4 r = philox4x32_10(make_uint4((uint32_t)(j >> 2), (uint32_t)row, (uint32_t)offset,
-                                           (uint32_t)(offset >> 32)),
-                                make_uint2((uint32_t)seed, (uint32_t)(seed >> 32)));
-  const uint32_t w = (j & 3) == 0 ? r.x : (j & 3) == 1 ? r.y : (j & 3) == 2 ? r.z : r.w;
-  const float u = ((float)(w >> 8) + 0.5f) * (1.0f / 16777216.0f);
-  return -logf(-logf(u));
-}
 
 template <typename E>
 __device__ __forceinline__ float to_float(E x);
@@ -123,7 +84,8 @@ __global__ void __launch_bounds__(S2_THREADS) decide_kernel(int rows, int chunks
                                                             const int* part_i, const int64_t* sampled,
                                                             const int64_t* draft, const int64_t* parent,
                                                             const int64_t* pos, int max_depth,
-                                                            int64_t* next_tokens, int64_t* result) {
+                                                            int64_t* next_tokens, int64_t* result,
+                                                            const int* upstream_err) {
   extern __shared__ __align__(16) uint8_t sm[];
   int64_t* nxt = reinterpret_cast<int64_t*>(sm);                  // [rows]
   int* par = reinterpret_cast<int*>(nxt + rows);                   // [rows]
@@ -133,6 +95,14 @@ __global__ void __launch_bounds__(S2_THREADS) decide_kernel(int rows, int chunks
   __shared__ int64_t red_v[S2_THREADS / 32];
   __shared__ int red_i[S2_THREADS / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (upstream_err && *upstream_err != 0) {   // the partials are not valid
+    for (int i = tid; i < rows; i += S2_THREADS) next_tokens[i] = -1;
+    if (tid == 0 && result) {
+      result[0] = TV_ERR_LAUNCH;
+      for (int k = 1; k < 8; ++k) result[k] = 0;
+    }
+    return;
+  }
   if (tid == 0) bad = 0;
 
   // 1. per-node target token
@@ -141,8 +111,21 @@ __global__ void __launch_bounds__(S2_THREADS) decide_kernel(int rows, int chunks
     if (sampled) {
       tok = sampled[i];
     } else {
+      // all of a lane's partials are loaded before they are compared, so the
+      // loads overlap instead of waiting one by one
       Best b{-INFINITY, 0x7fffffff};
-      for (int c = lane; c < chunks; c += 32) take(b, part_v[i * chunks + c], part_i[i * chunks + c]);
+      for (int c0 = 0; c0 < chunks; c0 += 32 * 8) {
+        float v[8];
+        int ix[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c = c0 + u * 32 + lane;
+          v[u] = c < chunks ? part_v[i * chunks + c] : -INFINITY;
+          ix[u] = c < chunks ? part_i[i * chunks + c] : 0x7fffffff;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) take(b, v[u], ix[u]);
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float v = __shfl_xor_sync(0xffffffffu, b.v, o);
@@ -156,6 +139,7 @@ __global__ void __launch_bounds__(S2_THREADS) decide_kernel(int rows, int chunks
       next_tokens[i] = tok;
     }
   }
+  if (!draft) return;   // next tokens only (uniform across the CTA)
   __syncthreads();
 
   // 2. parents over all rows (tree_verification.py:120-125) and first test
@@ -234,6 +218,24 @@ __global__ void __launch_bounds__(S2_THREADS) decide_kernel(int rows, int chunks
   }
 }
 
+}  // namespace
+
+int launch_accept_decide(int rows, int chunks, const float* part_v, const int* part_i, const int64_t* sampled,
+                         const int64_t* draft, const int64_t* parent, const int64_t* pos, int max_depth,
+                         int64_t* next_tokens, int64_t* result, const int* upstream_err, cudaStream_t st) {
+  const size_t smem = (size_t)rows * (sizeof(int64_t) + sizeof(int) + 2);
+  if (smem > 200 * 1024) return TV_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024) {
+    const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(decide_kernel), (int)smem);
+    if (rc_smem != TV_OK) return rc_smem;
+  }
+  decide_kernel<<<1, S2_THREADS, smem, st>>>(rows, chunks, part_v, part_i, sampled, draft, parent, pos, max_depth,
+                                             next_tokens, result, upstream_err);
+  return check_launch();
+}
+
+namespace {
+
 int choose_chunks(int rows, int vocab) {
   int c = (2 * kNumSMs + rows - 1) / rows;
   const int max_by_size = (vocab + 2047) / 2048;
@@ -305,15 +307,8 @@ int tv_accept(const tv_accept_args* a, void* stream) {
   } else if (!a->sampled) {
     return TV_ERR_NULL;
   }
-  const size_t smem = (size_t)rows * (sizeof(int64_t) + sizeof(int) + 2);
-  if (smem > 200 * 1024) return TV_ERR_UNSUPPORTED;
-  if (smem > 48 * 1024) {
-    const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(decide_kernel), (int)smem);
-    if (rc_smem != TV_OK) return rc_smem;
-  }
-  decide_kernel<<<1, S2_THREADS, smem, st>>>(rows, chunks, pv, pi, a->mode == 2 ? a->sampled : nullptr, a->draft,
-                                             a->parent, a->pos, a->max_depth, a->next_tokens, a->result);
-  return check_launch();
+  return launch_accept_decide(rows, chunks, pv, pi, a->mode == 2 ? a->sampled : nullptr, a->draft, a->parent, a->pos,
+                              a->max_depth, a->next_tokens, a->result, nullptr, st);
 }
 
 }  // extern "C"

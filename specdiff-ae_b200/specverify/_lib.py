@@ -86,6 +86,17 @@ class RopeArgs(ctypes.Structure):
     ]
 
 
+class LmheadArgs(ctypes.Structure):
+    """Mirror of ``tv_lmhead_args``."""
+    _fields_ = [
+        ("dtype", c_i32), ("rows", c_i32), ("hidden", c_i32), ("vocab", c_i32),
+        ("x", c_vp), ("x_sm", c_i64), ("weight", c_vp), ("w_sv", c_i64),
+        ("mode", c_i32), ("temperature", c_f32), ("seed", c_u64), ("offset", c_u64),
+        ("draft", c_vp), ("parent", c_vp), ("pos", c_vp), ("max_depth", c_i32),
+        ("next_tokens", c_vp), ("result", c_vp), ("workspace", c_vp), ("workspace_bytes", c_size),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGNATURES = {
     "tv_status_string": (ctypes.c_char_p, [c_i32]),
@@ -108,6 +119,8 @@ _SIGNATURES = {
                                 c_i32, c_i32, c_vp, c_i32, c_vp]),
     "tv_gather_page_table": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_i32, c_vp, c_vp]),
     "tv_rope_append": (c_i32, [ctypes.POINTER(RopeArgs), c_vp]),
+    "tv_lmhead_accept_workspace_size": (c_i32, [ctypes.POINTER(LmheadArgs), ctypes.POINTER(c_size)]),
+    "tv_lmhead_accept": (c_i32, [ctypes.POINTER(LmheadArgs), c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

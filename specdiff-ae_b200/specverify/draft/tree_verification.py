@@ -171,6 +171,65 @@ def accept(logits: Optional[torch.Tensor], draft: torch.Tensor, parent: torch.Te
     return AcceptResult(nxt, res, m)
 
 
+def accept_from_hidden(hidden: torch.Tensor, lm_head_weight: torch.Tensor, draft: Optional[torch.Tensor],
+                       parent: Optional[torch.Tensor], position_ids: Optional[torch.Tensor], max_depth: int, *,
+                       mode: str = "greedy", temperature: float = 1.0, seed: Optional[int] = None,
+                       offset: int = 0) -> AcceptResult:
+    """lm_head and acceptance in one pass: ``logits = hidden @ lm_head_weight.T``
+    (``diffspec_model.py:229-231``) is never materialised; each node's
+    argmax (or Gumbel-max sample at ``temperature``) over the logits rounded to
+    the weight's dtype feeds the acceptance rule of :func:`accept`
+    (``tree_verification.py:100-162``).
+
+    hidden [1, M, H] / [M, H] (M <= 128, H a multiple of 64), weight [V, H],
+    both bf16 or fp16.  With ``draft=None`` only ``next_tokens`` is filled.
+    The same ``seed`` / ``offset`` give the same samples as :func:`accept` on
+    the same rounded logits.
+    """
+    dev = _lib.require_cuda(hidden, lm_head_weight, draft)
+    x = hidden.reshape(-1, hidden.shape[-1])
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    w = lm_head_weight if lm_head_weight.stride(1) == 1 else lm_head_weight.contiguous()
+    if x.dtype != w.dtype:
+        raise _lib.SpecVerifyError(-2, f"hidden {x.dtype} and lm_head weight {w.dtype} differ")
+    if w.shape[1] != x.shape[1]:
+        raise _lib.SpecVerifyError(-1, f"weight {tuple(w.shape)} does not match hidden size {x.shape[1]}")
+    m = x.shape[0]
+    a = _lib.LmheadArgs()
+    a.dtype = _lib.dtype_code(x.dtype)
+    a.rows, a.hidden, a.vocab = m, x.shape[1], w.shape[0]
+    a.x, a.x_sm, a.weight, a.w_sv = x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0)
+    a.mode = {"greedy": MODE_GREEDY, "sample": MODE_SAMPLE}[mode]
+    keep = [x, w]
+    if draft is not None:
+        d = _i64(draft, dev)
+        if d.numel() != m:
+            raise _lib.SpecVerifyError(-1, f"hidden rows {m} != draft nodes {d.numel()}")
+        par = _i64(parent, dev) if m > 1 else torch.zeros(1, dtype=torch.int64, device=dev)
+        pos = _i64(position_ids.reshape(-1)[:m] if position_ids.dim() == 1 else position_ids[0], dev)
+        a.draft, a.parent, a.pos = d.data_ptr(), par.data_ptr(), pos.data_ptr()
+        a.max_depth = int(max_depth)
+        keep += [d, par, pos]
+    if a.mode == MODE_SAMPLE:
+        a.temperature = float(temperature)
+        if seed is None:
+            seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+        a.seed = int(seed) & (2 ** 64 - 1)
+        a.offset = int(offset) & (2 ** 64 - 1)
+    nxt = torch.empty(m, dtype=torch.int64, device=dev)
+    res = torch.zeros(RESULT_HEADER + 2 * m, dtype=torch.int64, device=dev)
+    a.next_tokens, a.result = nxt.data_ptr(), res.data_ptr()
+    lib = _lib.load()
+    need = ctypes.c_size_t(0)
+    _lib.check(lib.tv_lmhead_accept_workspace_size(ctypes.byref(a), ctypes.byref(need)),
+               "tv_lmhead_accept_workspace_size")
+    ws = torch.empty(max(int(need.value), 16), dtype=torch.uint8, device=dev)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(lib.tv_lmhead_accept(ctypes.byref(a), _lib.stream_ptr(dev)), "tv_lmhead_accept")
+    return AcceptResult(nxt, res, m)
+
+
 def compact_kv(past_key_values_data: List[torch.Tensor], start: int, acc: AcceptResult,
                max_rows: Optional[int] = None) -> None:
     """Move the accepted path's KV rows to ``[start, start + n)`` in every buffer.

@@ -64,7 +64,8 @@ def test_ctypes_structs_match_the_header(tmp_path):
         pytest.skip("no host C compiler")
     sys.path.insert(0, str(ROOT / "specdiff-ae_b200"))
     from specverify import _lib
-    mirrors = {"tv_attn_args": _lib.AttnArgs, "tv_accept_args": _lib.AcceptArgs, "tv_rope_args": _lib.RopeArgs}
+    mirrors = {"tv_attn_args": _lib.AttnArgs, "tv_accept_args": _lib.AcceptArgs, "tv_rope_args": _lib.RopeArgs,
+               "tv_lmhead_args": _lib.LmheadArgs}
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "specverify.h"', "int main(void) {"]
     for cname, py in mirrors.items():
         lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
