@@ -620,6 +620,81 @@ def run_lmhead(args):
     return res
 
 
+def run_tree(args):
+    """Final draft-tree build (the step that produces the verify inputs)."""
+    from specverify.runtime.draft_tree import finalize_tree
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --workload tree-finalize needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    nnodes, depth = 64, 8
+    g = torch.Generator(device="cpu").manual_seed(0)
+    pm = torch.randint(0, nnodes, (depth, nnodes), generator=g)
+    pm[0] = torch.arange(nnodes)
+    im = torch.randint(0, 128256, (depth, nnodes), generator=g)
+    top = torch.randperm(depth * nnodes, generator=g)[:nnodes]
+    pm, im, top = pm.to(dev), im.to(dev), top.to(dev)
+
+    def ours():
+        finalize_tree(top, pm, im, depth, nnodes, validate=False)
+
+    def reference_ops():
+        # DraftTree.update's final branch and generate_attention_mask
+        # (runtime/draft_tree.py:236-260, 188-215), then the root row / column
+        # (diffspec_model.py:620-624), as torch ops on the same GPU
+        rows = (top // nnodes).to(torch.long)
+        cols = (top % nnodes).to(torch.long)
+        order = torch.argsort(rows)
+        rows, cols = rows[order], cols[order]
+        k = nnodes
+        pos_table = torch.full((depth, nnodes), -1, dtype=torch.long, device=dev)
+        pos_table[rows, cols] = torch.arange(k, device=dev)
+        parent_pos = torch.full((k,), -1, dtype=torch.long, device=dev)
+        par_cols = pm[rows, cols]
+        has_parent = (rows > 0) & (par_cols >= 0)
+        if bool(has_parent.any()):
+            parent_pos[has_parent] = pos_table[rows[has_parent] - 1, par_cols[has_parent]]
+        attn = torch.zeros((k, k), dtype=torch.int8, device=dev)
+        diag = torch.arange(k, device=dev)
+        attn[diag, diag] = 1
+        cur = parent_pos
+        for _ in range(max(depth - 1, 0)):
+            valid = (cur >= 0) & (cur < k)
+            if not bool(valid.any()):
+                break
+            attn[diag[valid], cur[valid]] = 1
+            nxt = torch.full((k,), -1, dtype=torch.long, device=dev)
+            nxt[valid] = parent_pos[cur[valid]]
+            cur = nxt.clone()
+        ids = im[rows, cols]
+        m = torch.cat([torch.zeros(1, k, dtype=attn.dtype, device=dev), attn], dim=0)
+        m = torch.cat([torch.ones(k + 1, 1, dtype=attn.dtype, device=dev), m], dim=1)
+        return ids, rows + 1, parent_pos, m
+
+    us = _graph_us(ours, 20, args.steps, args.warmup)
+    for _ in range(args.warmup):
+        reference_ops()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reference_ops()
+    torch.cuda.synchronize()
+    ref_us = (time.perf_counter() - t0) * 1e6 / args.steps
+    return {
+        "metric": "draft-tree finalize latency", "value": round(us, 2), "unit": "us", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic (seeded random tree state)",
+        "config": {"workload": f"tree-finalize: {nnodes} nodes kept from {depth} depths, root-prepended verify "
+                               f"bitmask", "launch": "CUDA graph replays of the public API call"},
+        "roofline": {"bound": "latency", "achieved": round(us, 2), "peak": None, "unit": "us", "frac": None,
+                     "traffic": None, "kernel": "tree_finalize_kernel (one CTA, one launch)"},
+        "gpu_launches": args.steps * 20,
+        "reference_ops_on_gpu": {"us": round(ref_us, 1), "speedup": round(ref_us / us, 1),
+                                 "what": "the reference's final-branch torch ops on the same GPU (eager: it reads "
+                                         "a flag back to the host on every ancestor hop)"},
+    }
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -629,7 +704,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
-    ap.add_argument("--workload", choices=["verify", "rope-append", "lmhead-accept"], default="verify")
+    ap.add_argument("--workload", choices=["verify", "rope-append", "lmhead-accept", "tree-finalize"],
+                    default="verify")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -650,6 +726,10 @@ def main():
     if args.workload == "lmhead-accept":
         if rank == 0:
             print(json.dumps(run_lmhead(args)), file=_JSON_OUT, flush=True)
+        return
+    if args.workload == "tree-finalize":
+        if rank == 0:
+            print(json.dumps(run_tree(args)), file=_JSON_OUT, flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, rank, world)

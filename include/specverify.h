@@ -34,6 +34,12 @@
  *   tv_compact_paged      diffspec/core/kv_cache/paged_kv.py:168-223 (COW)
  *   tv_arena_gather       diffspec/core/kv_cache/chunk_arena.py:126-173
  *   tv_gather_page_table  diffspec/core/kv_cache/chunk_arena.py:86-178 (zero-copy form)
+ *   tv_rope_append        diffspec/runtime/llama_target_model.py:429-474 (RoPE)
+ *                         and diffspec/runtime/cache_state.py:52-66 (KVCache.cat)
+ *   tv_lmhead_accept      diffspec/draft/diffspec_model.py:229-231 (lm_head) and
+ *                         diffspec/draft/tree_verification.py:100-162
+ *   tv_tree_finalize      diffspec/runtime/draft_tree.py:188-260 and
+ *                         diffspec/draft/diffspec_model.py:620-624 (root prepend)
  */
 #ifndef SPECVERIFY_H_
 #define SPECVERIFY_H_
@@ -383,6 +389,27 @@ typedef struct tv_lmhead_args {
 
 int tv_lmhead_accept_workspace_size(const tv_lmhead_args* args, size_t* bytes);
 int tv_lmhead_accept(const tv_lmhead_args* args, void* stream);
+
+/* ---- final draft-tree build ---------------------------------------------------
+ * Replaces DraftTree.update's final branch and generate_attention_mask
+ * (runtime/draft_tree.py:188-260) -- the reference walks the ancestors with a
+ * host sync per hop -- plus the root row / column the verify step prepends
+ * (diffspec_model.py:620-624).  One CTA:
+ *   top_index [k] int64: the running top-k linear indices depth * nnodes + col;
+ *   parents_matrix / input_ids_matrix [>= depth, nnodes] int64 (row strides);
+ *   d2t [d2t_len] (optional): token = id + d2t[id] (draft -> target vocabulary).
+ * Nodes are ordered by depth, keeping the top-k order among equal depths.
+ * Outputs ([k] int64): input_ids, position_ids (= depth + 1), parent_pos (-1:
+ * none); mask (optional) [k, k] int8 self + ancestors (at most depth - 1
+ * hops); mask_bits (optional) [k + 1, ceil((k + 1) / 64)] uint64, the verify
+ * bitmask with the root prepended (root row: itself; root column: all).
+ * A top index outside [0, depth * nnodes), a repeated index or an id outside
+ * d2t sets *status (if given) to TV_ERR_INPUT. */
+int tv_tree_finalize(int32_t nnodes, int32_t depth, int32_t k, const int64_t* top_index,
+                     const int64_t* parents_matrix, int64_t pm_stride, const int64_t* input_ids_matrix,
+                     int64_t im_stride, const int64_t* d2t, int64_t d2t_len, int64_t* input_ids,
+                     int64_t* position_ids, int64_t* parent_pos, int8_t* mask, uint64_t* mask_bits,
+                     int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -22,4 +22,6 @@ arena       chunk-arena differential update
 bundles     branching-ancestor bundle grouping
 rope        rotary embedding of q / k and the KV-cache append (numpy, bit-exact
             emulation of the reference's bf16 / fp16 / fp32 element-wise ops)
+tree        final draft-tree build: node order, parent positions, ancestor
+            mask and the root-prepended verify bitmask
 """

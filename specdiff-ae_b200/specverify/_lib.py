@@ -121,6 +121,8 @@ _SIGNATURES = {
     "tv_rope_append": (c_i32, [ctypes.POINTER(RopeArgs), c_vp]),
     "tv_lmhead_accept_workspace_size": (c_i32, [ctypes.POINTER(LmheadArgs), ctypes.POINTER(c_size)]),
     "tv_lmhead_accept": (c_i32, [ctypes.POINTER(LmheadArgs), c_vp]),
+    "tv_tree_finalize": (c_i32, [c_i32, c_i32, c_i32, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp,
+                                 c_vp, c_vp, c_vp, c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

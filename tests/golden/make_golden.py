@@ -32,6 +32,11 @@ bundles.json
     ``BundleScheduler.schedule_bundles`` on seeded trees.
 bundle_verify.npz
     ``FusedBundleVerifier`` torch path.
+tree_final.npz
+    ``DraftTree`` (``runtime/draft_tree.py``) driven with seeded draft
+    distributions to its depth limit: the final state (running top-k
+    indices, per-depth parents and tokens) and ``update``'s final outputs
+    (tokens, positions, ancestor mask, parent positions), several sizes.
 rope_bf16.npz / rope_f16.npz / rope_f32.npz
     ``LlamaRotaryEmbedding`` (theta 500000) cached cos/sin tables,
     ``apply_rotary_pos_emb`` with tree position ids, ``apply_rotary_pos_emb_L31``
@@ -395,11 +400,38 @@ def gen_rope(ltm, dtype, path: Path):
         k_states_len=k_states.shape[2], v_states_len=v_states.shape[2])
 
 
+def gen_tree(path: Path):
+    from diffspec.runtime import draft_tree as dt                 # noqa: E402
+    out = {}
+    cases = [(16, 5, 4, 500), (64, 8, 8, 1000), (64, 10, 3, 300), (8, 3, 2, 50)]
+    for ci, (nnodes, max_depth, seed, vocab) in enumerate(cases):
+        gen = torch.Generator().manual_seed(seed)
+        tree = dt.DraftTree(nnodes, "cpu", threshold=-1e30, max_depth=max_depth)
+        res = tree.update(torch.softmax(torch.randn(1, 3, vocab, generator=gen), -1))
+        while not res["is_final"]:
+            res = tree.update(torch.softmax(torch.randn(1, nnodes, vocab, generator=gen), -1))
+        top = tree._run_top_idx.clone()
+        rows = (top // nnodes).numpy()
+        # the final ordering is torch.argsort(rows); record whether it kept the
+        # top-k order among equal depths (the GPU sort the reference runs does)
+        ref_order = torch.argsort(top // nnodes).numpy()            # the same call update() made
+        stable = np.array_equal(np.argsort(rows, kind="stable"), ref_order)
+        p = f"c{ci}_"
+        out.update({p + "nnodes": nnodes, p + "depth": tree.depth, p + "top_index": top.numpy(),
+                    p + "parents_matrix": tree.parents_matrix.numpy(),
+                    p + "input_ids_matrix": tree.input_ids_matrix.numpy(),
+                    p + "input_ids": res["input_ids"].numpy(), p + "position_ids": res["position_ids"].numpy(),
+                    p + "attention_mask": res["attention_mask"].numpy(), p + "parent_last": res["parent_last"].numpy(),
+                    p + "argsort_stable": stable, p + "ref_order": ref_order})
+    out["cases"] = len(cases)
+    np.savez_compressed(path, **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DIFFSPEC_REFERENCE", "/root/reference"))
     ap.add_argument("--only", default="", help="comma-separated subset: attention, accept, paged, arena, "
-                                               "bundles, bundle_verify, rope")
+                                               "bundles, bundle_verify, rope, tree")
     args = ap.parse_args()
     only = set(filter(None, args.only.split(",")))
     want = (lambda name: not only or name in only)
@@ -418,6 +450,8 @@ def main():
         gen_bundles(bs, HERE / "bundles.json")
     if want("bundle_verify"):
         gen_bundle_verify(bv, HERE / "bundle_verify.npz")
+    if want("tree"):
+        gen_tree(HERE / "tree_final.npz")
     if want("rope"):
         gen_rope(ltm, torch.bfloat16, HERE / "rope_bf16.npz")
         gen_rope(ltm, torch.float16, HERE / "rope_f16.npz")

@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from conftest import bf16_from_bits, load_golden
-from oracle import acceptance, arena, attention, bundles, paged, rope
+from oracle import acceptance, arena, attention, bundles, paged, rope, tree
 
 
 def _t(x, dtype):
@@ -243,3 +243,21 @@ def test_rope_table_matches_reference_cast():
     got = rope.round_to(cos, "bf16")
     ref = bf16_from_bits(z["cos"])
     assert np.mean(got == ref) > 0.999
+
+
+def test_tree_oracle_matches_reference():
+    z = load_golden("tree_final.npz")
+    for c in range(int(z["cases"])):
+        p = f"c{c}_"
+        out = tree.finalize(z[p + "top_index"], z[p + "parents_matrix"], z[p + "input_ids_matrix"],
+                            int(z[p + "depth"]), int(z[p + "nnodes"]), order=z[p + "ref_order"])
+        for key in ("input_ids", "position_ids", "attention_mask", "parent_last"):
+            np.testing.assert_array_equal(out[key], z[p + key], err_msg=f"case {c} {key}")
+
+
+def test_tree_verify_mask_and_bits():
+    m = np.array([[1, 0, 0], [1, 1, 0], [1, 0, 1]], dtype=np.int8)
+    v = tree.verify_mask(m)
+    assert v.tolist() == [[1, 0, 0, 0], [1, 1, 0, 0], [1, 1, 1, 0], [1, 1, 0, 1]]
+    bits = tree.pack_bits(v)
+    assert [int(b) for b in bits[:, 0]] == [0b1, 0b11, 0b111, 0b1011]
