@@ -695,6 +695,75 @@ def run_tree(args):
     }
 
 
+def run_retrieve(args):
+    """Draft-side chunk retrieval: selection + working-cache gather (config 5 sizes)."""
+    from specverify.draft.retrieval import GatherPlan, gather_rows, select_chunks
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --workload chunk-retrieve needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    length, cs, k, heads, d = 262144, 2048, 32, 8, 128
+    g = torch.Generator(device="cpu").manual_seed(0)
+    attn = torch.rand(length, generator=g).to(dev)
+    starts = torch.arange(0, length, cs, device=dev)
+    ends = starts + cs
+    full = [(torch.randn(1, heads, length, d, generator=g).bfloat16().to(dev),
+             torch.randn(1, heads, length, d, generator=g).bfloat16().to(dev))]
+    rows = k * cs                                 # the working cache's length for disjoint chunks
+    plan = GatherPlan(full, rows)
+
+    def ours():
+        sel, idx, count = select_chunks(attn, starts, ends, k, length, validate=False)
+        gather_rows(plan, idx, count)
+
+    def reference_ops():
+        # draft_network.py:1524-1594 as torch ops on the same GPU (with its host reads)
+        cum = torch.cumsum(attn, dim=0)
+        lower = torch.zeros_like(starts, dtype=cum.dtype)
+        mask_pos = starts > 0
+        if bool(mask_pos.any()):
+            lower[mask_pos] = cum.index_select(0, (starts[mask_pos] - 1).clamp_(min=0, max=length - 1))
+        upper = cum.index_select(0, (ends - 1).clamp_(min=0, max=length - 1))
+        score = (upper - lower) / (ends - starts).clamp_min(1).to(cum.dtype)
+        selected = torch.sort(torch.topk(score, k=k, dim=0).indices)[0]
+        _ = selected.tolist()
+        diff = torch.zeros(length + 1, dtype=torch.int32, device=dev)
+        diff.index_add_(0, starts.index_select(0, selected).clamp_(0, length),
+                        torch.ones(k, dtype=torch.int32, device=dev))
+        diff.index_add_(0, ends.index_select(0, selected).clamp_(0, length),
+                        -torch.ones(k, dtype=torch.int32, device=dev))
+        idx = torch.nonzero(torch.cumsum(diff[:length], dim=0) > 0, as_tuple=False).squeeze(1)
+        return [(fk.index_select(2, idx).contiguous(), fv.index_select(2, idx).contiguous()) for fk, fv in full]
+
+    us = _graph_us(ours, 5, args.steps, args.warmup)
+    for _ in range(args.warmup):
+        reference_ops()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reference_ops()
+    torch.cuda.synchronize()
+    ref_us = (time.perf_counter() - t0) * 1e6 / args.steps
+    alg = 2 * 2 * heads * rows * d * 2 + length * 4          # K and V rows read + written, the scores read
+    peak, kind = peaks()
+    gbs = alg / (us * 1e-6) / 1e9
+    return {
+        "metric": "chunk retrieval GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded uniform scores, N(0,1) K/V)",
+        "config": {"workload": f"chunk-retrieve: {length} draft tokens in {cs}-token chunks, top {k} chunks, one "
+                               f"draft layer's K/V ({heads} heads, head_dim {d}) gathered",
+                   "launch": "CUDA graph replays of the public API calls", "algorithmic_bytes_per_step": alg},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "traffic": None, "peak_kind": kind,
+                     "kernel": "chunk_select_kernel + gather_rows_kernel (two launches per call)"},
+        "gpu_launches": args.steps * 5 * 2,
+        "reference_ops_on_gpu": {"us": round(ref_us, 1), "speedup": round(ref_us / us, 2),
+                                 "what": "the reference's retrieval ops on the same GPU (eager: it reads the "
+                                         "selection back to the host)"},
+    }
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -704,8 +773,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
-    ap.add_argument("--workload", choices=["verify", "rope-append", "lmhead-accept", "tree-finalize"],
-                    default="verify")
+    ap.add_argument("--workload", choices=["verify", "rope-append", "lmhead-accept", "tree-finalize",
+                                           "chunk-retrieve"], default="verify")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -730,6 +799,10 @@ def main():
     if args.workload == "tree-finalize":
         if rank == 0:
             print(json.dumps(run_tree(args)), file=_JSON_OUT, flush=True)
+        return
+    if args.workload == "chunk-retrieve":
+        if rank == 0:
+            print(json.dumps(run_retrieve(args)), file=_JSON_OUT, flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, rank, world)

@@ -40,6 +40,8 @@
  *                         diffspec/draft/tree_verification.py:100-162
  *   tv_tree_finalize      diffspec/runtime/draft_tree.py:188-260 and
  *                         diffspec/draft/diffspec_model.py:620-624 (root prepend)
+ *   tv_chunk_select,
+ *   tv_gather_rows        diffspec/draft/draft_network.py:1514-1612 (retrieval)
  */
 #ifndef SPECVERIFY_H_
 #define SPECVERIFY_H_
@@ -405,6 +407,34 @@ int tv_lmhead_accept(const tv_lmhead_args* args, void* stream);
  * bitmask with the root prepended (root row: itself; root column: all).
  * A top index outside [0, depth * nnodes), a repeated index or an id outside
  * d2t sets *status (if given) to TV_ERR_INPUT. */
+/* ---- draft-side chunk retrieval ------------------------------------------------
+ * Replaces the retrieval branch of DraftNetwork._select_working_cache_from_chunks
+ * (draft/draft_network.py:1514-1612; no semantic penalty).
+ * tv_chunk_select (one CTA): chunk score = (attention summed over the chunk,
+ *   prefix indices clamped to attn_len as the reference's prefix sums are) /
+ *   max(end - start, 1); the top_k best (NaN largest, ties to the smaller id)
+ *   in ascending id order into selected[top_k]; the union of their
+ *   [start, end) intervals clamped to [0, length] as ascending token indices
+ *   into indices[max_indices], their number into *count.  nchunks <= 2048,
+ *   top_k <= 1024.  More than max_indices indices, or a chunk bound < 0, sets
+ *   *status to TV_ERR_INPUT (then nothing is written past max_indices).
+ *   workspace: tv_chunk_select_workspace_size bytes (per-chunk sums).
+ * tv_gather_rows: for every plane p < planes (src[p], dst[p]: device
+ *   pointers, e.g. each layer's K and V), every head h < heads and every
+ *   i < *count (at most max_rows): copy row_bytes from src[p] + h *
+ *   src_head_stride_bytes + indices[i] * src_row_stride_bytes to dst[p] + h *
+ *   dst_head_stride_bytes + i * dst_row_stride_bytes.  row_bytes a multiple
+ *   of 16, 16-byte aligned rows. */
+int tv_chunk_select_workspace_size(int32_t nchunks, int64_t attn_len, size_t* bytes);
+int tv_chunk_select(const float* attn, int64_t attn_len, const int64_t* starts, const int64_t* ends,
+                    int32_t nchunks, int32_t top_k, int64_t length, int64_t* selected, int64_t* indices,
+                    int64_t max_indices, int64_t* count, void* workspace, size_t workspace_bytes,
+                    int32_t* status, void* stream);
+int tv_gather_rows(int32_t planes, int32_t heads, const uint64_t* src, const uint64_t* dst,
+                   int64_t src_head_stride_bytes, int64_t src_row_stride_bytes, int64_t dst_head_stride_bytes,
+                   int64_t dst_row_stride_bytes, int32_t row_bytes, const int64_t* indices, const int64_t* count,
+                   int64_t max_rows, void* stream);
+
 int tv_tree_finalize(int32_t nnodes, int32_t depth, int32_t k, const int64_t* top_index,
                      const int64_t* parents_matrix, int64_t pm_stride, const int64_t* input_ids_matrix,
                      int64_t im_stride, const int64_t* d2t, int64_t d2t_len, int64_t* input_ids,

@@ -24,4 +24,5 @@ rope        rotary embedding of q / k and the KV-cache append (numpy, bit-exact
             emulation of the reference's bf16 / fp16 / fp32 element-wise ops)
 tree        final draft-tree build: node order, parent positions, ancestor
             mask and the root-prepended verify bitmask
+retrieval   draft-side chunk scores, top-k, interval union and row gather
 """

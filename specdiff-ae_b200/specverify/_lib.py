@@ -123,6 +123,10 @@ _SIGNATURES = {
     "tv_lmhead_accept": (c_i32, [ctypes.POINTER(LmheadArgs), c_vp]),
     "tv_tree_finalize": (c_i32, [c_i32, c_i32, c_i32, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp,
                                  c_vp, c_vp, c_vp, c_vp]),
+    "tv_chunk_select_workspace_size": (c_i32, [c_i32, c_i64, ctypes.POINTER(c_size)]),
+    "tv_chunk_select": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp, c_size,
+                                c_vp, c_vp]),
+    "tv_gather_rows": (c_i32, [c_i32, c_i32, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

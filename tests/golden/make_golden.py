@@ -37,6 +37,11 @@ tree_final.npz
     distributions to its depth limit: the final state (running top-k
     indices, per-depth parents and tokens) and ``update``'s final outputs
     (tokens, positions, ancestor mask, parent positions), several sizes.
+retrieval.npz
+    ``DraftNetwork._select_working_cache_from_chunks`` (retrieval mode) on a
+    stand-in object holding its inputs: per-token attention scores (dyadic
+    values, so every prefix sum is exact), chunk bounds, top-k; the selected
+    chunk ids, the interval-union token indices and the gathered working K/V.
 rope_bf16.npz / rope_f16.npz / rope_f32.npz
     ``LlamaRotaryEmbedding`` (theta 500000) cached cos/sin tables,
     ``apply_rotary_pos_emb`` with tree position ids, ``apply_rotary_pos_emb_L31``
@@ -427,11 +432,52 @@ def gen_tree(path: Path):
     np.savez_compressed(path, **out)
 
 
+def gen_retrieval(path: Path):
+    import types
+    from diffspec.draft import draft_network as dn                 # noqa: E402
+    out = {}
+    # (L, chunk size, top-k, layers, heads, head_dim, overlapping chunks)
+    cases = [(1000, 32, 7, 2, 2, 16, False), (4096, 256, 5, 1, 2, 8, False), (300, 64, 9, 1, 1, 8, False),
+             (777, 50, 4, 2, 2, 8, True)]
+    for ci, (L, cs, topk, layers, heads, d, overlap) in enumerate(cases):
+        gen = torch.Generator().manual_seed(100 + ci)
+        starts = list(range(0, L, cs))
+        ends = [min(s0 + cs, L) for s0 in starts]
+        if overlap:                                # chunks reaching into the next one
+            ends = [min(e + cs // 3, L) for e in ends]
+        chunks = [(i, s0, e) for i, (s0, e) in enumerate(zip(starts, ends))]
+        # multiples of 2^-12 below 1: every partial sum is exact in fp32
+        attn = torch.randint(0, 4096, (L,), generator=gen).float() / 4096.0
+        # K/V values k / 16 with |k| < 256: exact in fp16, stored as fp16
+        full_kv = [(torch.randint(-255, 256, (1, heads, L, d), generator=gen).float() / 16,
+                    torch.randint(-255, 256, (1, heads, L, d), generator=gen).float() / 16) for _ in range(layers)]
+        st = types.SimpleNamespace(
+            full_draft_kv=full_kv, total_seq_len=L, chunks=chunks, selected_chunks=chunks[:1],
+            retrieve_top_k=topk, attn_scores_final=attn.clone(), attn_scores=None, retrieval_condition=True,
+            _chunks_starts=torch.tensor(starts), _chunks_ends=torch.tensor(ends), _diff_buf=None, _ones_buf=None,
+            gamma_sem=0.0, prev_selected_chunk_ids=[], chunk_arena=None,
+            past_key_position_ids=torch.arange(L).unsqueeze(0), evicted=0, retrieval_verbose=False)
+        st._record_chunk_overlap_ratio = lambda a, b: None
+        st.update_working_cache_from_full = lambda: None
+        working = dn.DraftNetwork._select_working_cache_from_chunks(st, top_k_chunks=topk, do_retrieval=True)
+        n_ret = working[0][0].shape[2]
+        p = f"c{ci}_"
+        out.update({p + "L": L, p + "top_k": topk, p + "attn": attn.numpy(), p + "starts": np.array(starts),
+                    p + "ends": np.array(ends), p + "selected": np.array(st.prev_selected_chunk_ids),
+                    p + "n_ret": n_ret, p + "evicted": st.evicted})
+        for li, ((fk, fv), (wk, wv)) in enumerate(zip(full_kv, working)):
+            out.update({p + f"full_k{li}": fk.numpy().astype(np.float16), p + f"full_v{li}": fv.numpy().astype(np.float16),
+                        p + f"work_k{li}": wk.numpy().astype(np.float16), p + f"work_v{li}": wv.numpy().astype(np.float16)})
+        out[p + "layers"] = layers
+    out["cases"] = len(cases)
+    np.savez_compressed(path, **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("DIFFSPEC_REFERENCE", "/root/reference"))
     ap.add_argument("--only", default="", help="comma-separated subset: attention, accept, paged, arena, "
-                                               "bundles, bundle_verify, rope, tree")
+                                               "bundles, bundle_verify, rope, tree, retrieval")
     args = ap.parse_args()
     only = set(filter(None, args.only.split(",")))
     want = (lambda name: not only or name in only)
@@ -450,6 +496,8 @@ def main():
         gen_bundles(bs, HERE / "bundles.json")
     if want("bundle_verify"):
         gen_bundle_verify(bv, HERE / "bundle_verify.npz")
+    if want("retrieval"):
+        gen_retrieval(HERE / "retrieval.npz")
     if want("tree"):
         gen_tree(HERE / "tree_final.npz")
     if want("rope"):

@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from conftest import bf16_from_bits, load_golden
-from oracle import acceptance, arena, attention, bundles, paged, rope, tree
+from oracle import acceptance, arena, attention, bundles, paged, retrieval, rope, tree
 
 
 def _t(x, dtype):
@@ -261,3 +261,15 @@ def test_tree_verify_mask_and_bits():
     assert v.tolist() == [[1, 0, 0, 0], [1, 1, 0, 0], [1, 1, 1, 0], [1, 1, 0, 1]]
     bits = tree.pack_bits(v)
     assert [int(b) for b in bits[:, 0]] == [0b1, 0b11, 0b111, 0b1011]
+
+
+def test_retrieval_oracle_matches_reference():
+    z = load_golden("retrieval.npz")
+    for c in range(int(z["cases"])):
+        p = f"c{c}_"
+        sel, idx = retrieval.select(z[p + "attn"], z[p + "starts"], z[p + "ends"], int(z[p + "top_k"]), int(z[p + "L"]))
+        np.testing.assert_array_equal(sel, z[p + "selected"], err_msg=f"case {c}")
+        assert idx.size == int(z[p + "n_ret"]) and int(z[p + "L"]) - idx.size == int(z[p + "evicted"])
+        for li in range(int(z[p + "layers"])):
+            np.testing.assert_array_equal(retrieval.gather(z[p + f"full_k{li}"], idx), z[p + f"work_k{li}"])
+            np.testing.assert_array_equal(retrieval.gather(z[p + f"full_v{li}"], idx), z[p + f"work_v{li}"])
