@@ -12,9 +12,9 @@ heads, head_dim 128), bf16.  Steps rotate over 4 independent layer pools
 
 N = 1 runs config 2 on one GPU.  N > 1 (torchrun, one rank per GPU) runs the
 same 64K problem sequence-sharded: each rank attends its contiguous share of
-the pages, and one NCCL all_gather of the packed (O, lse) partials plus a
-local log-sum-exp merge gives every rank the full result ("scaling":
-"strong": total work fixed).  Time = max over ranks of CUDA-event time.
+the pages; one kernel per rank then pushes its (O, lse) partial into every
+peer's buffer over NVLink and merges all ranks' partials by log-sum-exp, so
+every rank holds the full result ("scaling": "strong": total work fixed).  Time = max over ranks of CUDA-event time.
 
 `value` = algorithmic bytes (every visible K/V row once + Q/O/LSE/page
 table/bitmask) / step time, in GB/s, whole job.  `e2e` measures the same call
@@ -188,16 +188,16 @@ def run_ours(args, rank, world, dev):
             p = probs[i % rotate]
             verifier(p.q, p.k_pool, p.v_pool, shard_len, bits[i % rotate] if rank == world - 1 else None,
                      page_table=shards[i % rotate])
-        launches_per_step = 3
+        launches_per_step = 2
         workload = (f"config2 sequence-sharded over {world} GPUs: S=65536 paged, 64-node depth-8 tree, 1 layer, "
-                    f"bf16, one NCCL all_gather of (O, lse) partials + LSE merge per step")
+                    f"bf16, partials pushed to every peer over NVLink and merged by one fused kernel per step")
 
     for _ in range(args.warmup):
         for i in range(rotate):
             step(i)
     torch.cuda.synchronize()
     # The timed steps replay CUDA graphs of the launch sequence (one per
-    # rotated problem; the sharded step's NCCL all_gather included), so the
+    # rotated problem; the sharded step's peer exchange included), so the
     # device time is not bounded by Python launch overhead.
     graphs = []
     if not args.no_graph:

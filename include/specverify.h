@@ -169,24 +169,36 @@ int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
                       const float* parts_lse, int64_t part_stride_lse,
                       int32_t out_dtype, void* out, float* out_lse, void* stream);
 
-/* ---- sequence-sharded exchange over NVLink peer memory --------------------
- * No counterpart in the reference (it has no multi-GPU verify).  Each rank's
- * buffer, mapped into every rank, holds two partial slots
- *   slot s at byte s * slot_bytes: O [rows][head_dim] fp32, then lse [rows]
- * and, at flag_offset, int32 words [flag 0, flag 1, ready, finished], all
- * zero before the first step; `counter` (this rank's step count, zero
- * initially) is device memory of this rank.  tv_peer_merge, after this
- * rank's partial was written on `stream`: publishes flags[slot] = step with a
- * system-scope release, waits (bounded, 2 s; then *status = 8 and NaN rows)
- * until every peer's flags[slot] reaches the step, merges all ranks' slot
- * partials (read over NVLink) by log-sum-exp in rank order into
- * out [rows][head_dim] (out_dtype) and out_lse [rows] (optional), and
- * advances the counter.  bases[r] = rank r's buffer as mapped in this
- * process (world <= 8).  Successive steps must alternate the slot. */
-int tv_peer_merge(int32_t world, int32_t rank, const void* const* bases, int64_t slot_bytes,
-                  int32_t slot, int64_t flag_offset, int32_t* counter, int64_t rows,
-                  int32_t head_dim, int32_t out_dtype, void* out, float* out_lse,
-                  int32_t* status, void* stream);
+/* ---- sequence-sharded verify over NVLink peer memory ---------------------
+ * No counterpart in the reference (it attends the whole prefix on one device,
+ * llama_target_model.py:839-845, and has no multi-GPU code).  One process per
+ * GPU; each rank holds a contiguous shard of the keys (the rank holding the
+ * tree also its M tree keys and the bitmask).
+ *
+ * Exchange buffer: tv_sharded_exchange_bytes(world, rows, head_dim) bytes per
+ * rank, rows = batch * heads * rows_per_sequence (query rows), allocated so
+ * that every rank can address every other rank's buffer (symmetric / IPC
+ * memory), 16-byte aligned and zeroed before the first step.  It holds two
+ * slots of `world` fp32 partials (O and LSE), per-row-block arrival flags and
+ * this rank's step count.
+ *
+ * tv_verify_attn_sharded: `args` is this rank's request exactly as for
+ * tv_verify_attn (args->num_keys = this shard's keys) except that out / lse /
+ * aux_lse / weight receive the MERGED result over all ranks' shards, and
+ * args->workspace holds this rank's split partials
+ * (tv_verify_attn_sharded_workspace_size bytes).  It launches the attention
+ * kernel, then one kernel that combines this rank's split partials, stores
+ * them into every peer's buffer, publishes per-row-block flags with a
+ * system-scope release, waits on its own buffer for the peers' (bounded:
+ * 2 s, then *args->status = 8 and NaN rows) and merges all ranks' partials by
+ * log-sum-exp in rank order: every rank gets bit-identical outputs.
+ * bases[r] = rank r's exchange buffer as mapped in this process (world <= 8).
+ * Every rank must make the same sequence of calls with the same shapes;
+ * successive calls alternate the buffer's two slots by themselves. */
+int tv_sharded_exchange_bytes(int32_t world, int64_t rows, int32_t head_dim, int64_t* bytes);
+int tv_verify_attn_sharded_workspace_size(const tv_attn_args* args, size_t* bytes);
+int tv_verify_attn_sharded(const tv_attn_args* args, int32_t world, int32_t rank, const void* const* bases,
+                           void* stream);
 
 /* ---- masks --------------------------------------------------------------
  * Pack a [batch][rows][cols] keep-mask into bits: bit c of row r is set when

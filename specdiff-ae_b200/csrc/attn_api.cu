@@ -44,14 +44,10 @@ int ensure_dynamic_smem(const void* kernel, int bytes) {
 namespace {
 
 // ---- split combine: D/4 threads per query row, one float4 of O each --------
-// Partials are read up to 8 splits at a time (all loads of a block in flight
-// together, they are usually still in L2) and folded with a running max, so
-// the row needs one pass.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) {
   constexpr int TPR = D / 4;          // threads per row
   constexpr int RPB = 128 / TPR;      // rows per block
-  constexpr int BLK = 8;              // splits loaded together
   const int q = threadIdx.x % TPR;
   const int64_t row = (int64_t)blockIdx.x * RPB + threadIdx.x / TPR;
   const int64_t total = (int64_t)p.B * p.Hkv * p.R;
@@ -60,51 +56,13 @@ __global__ void __launch_bounds__(128) split_combine_kernel(const AttnParams p) 
   const int r = (int)(row - (int64_t)bh * p.R);
   const int b = bh / p.Hkv;
   const int hk = bh - b * p.Hkv;
-
-  float mx = -INFINITY, wsum = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s0 = 0; s0 < p.splits; s0 += BLK) {
-    float l[BLK];
-    float4 v[BLK];
-#pragma unroll
-    for (int j = 0; j < BLK; ++j) {
-      const int s = s0 + j;
-      if (s < p.splits) {
-        l[j] = *part_lse_row(p, s, bh, r);
-        v[j] = *reinterpret_cast<const float4*>(part_o_row(p, s, bh, r, D) + 4 * q);
-      } else {
-        l[j] = -INFINITY;
-        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    float bm = l[0];
-#pragma unroll
-    for (int j = 1; j < BLK; ++j) bm = fmaxf(bm, l[j]);
-    const float nm = fmaxf(mx, bm);
-    if (nm == -INFINITY) continue;
-    const float sc = mx == -INFINITY ? 0.f : expf(mx - nm);
-    acc.x *= sc;
-    acc.y *= sc;
-    acc.z *= sc;
-    acc.w *= sc;
-    wsum *= sc;
-#pragma unroll
-    for (int j = 0; j < BLK; ++j) {
-      const float w = l[j] == -INFINITY ? 0.f : expf(l[j] - nm);
-      wsum += w;
-      acc.x += w * v[j].x;
-      acc.y += w * v[j].y;
-      acc.z += w * v[j].z;
-      acc.w += w * v[j].w;
-    }
-    mx = nm;
-  }
-  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-  const float lse = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+  float4 o;
+  float lse;
+  combine_split_row<D>(p, bh, r, q, o, lse);
   int m, h;
   row_coords(p, hk, r, m, h);
-  store_out_pair<T>(p, b, m, h, 4 * q, acc.x * inv, acc.y * inv);
-  store_out_pair<T>(p, b, m, h, 4 * q + 2, acc.z * inv, acc.w * inv);
+  store_out_pair<T>(p, b, m, h, 4 * q, o.x, o.y);
+  store_out_pair<T>(p, b, m, h, 4 * q + 2, o.z, o.w);
   if (q == 0) store_row_stats<T>(p, b, m, h, lse);
 }
 
@@ -222,13 +180,71 @@ Plan plan(const tv_attn_args* a) {
   return pl;
 }
 
-size_t workspace_for(const tv_attn_args* a, const Plan& pl) {
-  if (pl.splits <= 1) return 0;
+// Bytes of `splits` partials: O [splits][rows][D] fp32 (256-byte aligned end),
+// then LSE [splits][rows] fp32.
+size_t partial_bytes(const tv_attn_args* a, int splits) {
   const int G = a->heads / a->kv_heads;
   const int64_t rows = (int64_t)a->batch * a->kv_heads * a->rows * G;
-  const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);
-  const size_t l = (size_t)pl.splits * rows * sizeof(float);
+  const size_t o = (size_t)splits * rows * a->head_dim * sizeof(float);
+  const size_t l = (size_t)splits * rows * sizeof(float);
   return ((o + 255) & ~size_t(255)) + l;
+}
+
+size_t workspace_for(const tv_attn_args* a, const Plan& pl) {
+  return pl.splits <= 1 ? 0 : partial_bytes(a, pl.splits);
+}
+
+// Kernel parameters of a validated request; partials (when `partials`) in
+// a->workspace.
+void fill_params(const tv_attn_args* a, const Plan& pl, bool partials, AttnParams& p) {
+  memset(&p, 0, sizeof(p));
+  p.q = a->q;
+  p.q_sb = a->q_sb; p.q_sm = a->q_sm; p.q_sh = a->q_sh;
+  p.k = a->k ? a->k : a->q;
+  p.v = a->v ? a->v : a->q;
+  p.k_sb = a->k_sb; p.k_sn = a->k_sn; p.k_sh = a->k_sh;
+  p.v_sb = a->v_sb; p.v_sn = a->v_sn; p.v_sh = a->v_sh;
+  p.pt = a->page_table;
+  p.pt_sb = a->pt_sb;
+  p.page_shift = 0;
+  if (a->page_table) while ((1 << p.page_shift) < a->page_size) ++p.page_shift;
+  p.num_pages = a->num_pages;
+  p.kv_lens = a->kv_lens;
+  p.num_keys = a->num_keys;
+  p.mask_len = a->mask_len;
+  p.mask = a->mask;
+  p.mask_sb = a->mask_sb; p.mask_sm = a->mask_sm;
+  p.B = a->batch; p.M = a->rows; p.H = a->heads; p.Hkv = a->kv_heads;
+  p.G = a->heads / a->kv_heads;
+  p.R = a->rows * p.G;
+  p.scale_log2 = a->scale * kLog2e;
+  p.splits = pl.splits;
+  p.tiles_per_split = pl.tiles_per_split;
+  p.out = a->out;
+  p.o_sb = a->o_sb; p.o_sm = a->o_sm; p.o_sh = a->o_sh;
+  p.out_f32 = a->out_f32;
+  p.lse = a->lse;
+  p.lse_sb = a->lse_sb; p.lse_sm = a->lse_sm; p.lse_sh = a->lse_sh;
+  p.aux = a->aux_lse;
+  p.aux_sb = a->aux_sb; p.aux_sm = a->aux_sm; p.aux_sh = a->aux_sh;
+  p.weight = a->weight;
+  p.w_sb = a->w_sb; p.w_sm = a->w_sm; p.w_sh = a->w_sh;
+  p.err = a->status;
+  p.trace = g_trace;
+  if (partials) {
+    const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
+    const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);
+    p.part_o = static_cast<float*>(a->workspace);
+    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + ((o + 255) & ~size_t(255)));
+  }
+}
+
+// Short key ranges take the split-P PV product (see attn_mma.cu); long ones
+// average the bf16 rounding of P away.  Bit 4 of `kernel` forces it.
+int launch_attention(const tv_attn_args* a, const Plan& pl, const AttnParams& p, cudaStream_t st) {
+  const bool precise = (a->kernel & 16) || a->num_keys <= kPreciseMaxKeys;
+  return pl.tc ? launch_attn_tc(p, a->dtype, a->head_dim, st)
+               : launch_attn_mma(p, a->dtype, a->head_dim, precise, st);
 }
 
 }  // namespace
@@ -292,57 +308,46 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
   const size_t need = workspace_for(a, pl);
   if (need > 0 && (!a->workspace || a->workspace_bytes < need)) return TV_ERR_WORKSPACE;
   if (need > 0 && !aligned16(a->workspace)) return TV_ERR_ALIGN;
-
   AttnParams p;
-  memset(&p, 0, sizeof(p));
-  p.q = a->q;
-  p.q_sb = a->q_sb; p.q_sm = a->q_sm; p.q_sh = a->q_sh;
-  p.k = a->k ? a->k : a->q;
-  p.v = a->v ? a->v : a->q;
-  p.k_sb = a->k_sb; p.k_sn = a->k_sn; p.k_sh = a->k_sh;
-  p.v_sb = a->v_sb; p.v_sn = a->v_sn; p.v_sh = a->v_sh;
-  p.pt = a->page_table;
-  p.pt_sb = a->pt_sb;
-  p.page_shift = 0;
-  if (a->page_table) while ((1 << p.page_shift) < a->page_size) ++p.page_shift;
-  p.num_pages = a->num_pages;
-  p.kv_lens = a->kv_lens;
-  p.num_keys = a->num_keys;
-  p.mask_len = a->mask_len;
-  p.mask = a->mask;
-  p.mask_sb = a->mask_sb; p.mask_sm = a->mask_sm;
-  p.B = a->batch; p.M = a->rows; p.H = a->heads; p.Hkv = a->kv_heads;
-  p.G = a->heads / a->kv_heads;
-  p.R = a->rows * p.G;
-  p.scale_log2 = a->scale * kLog2e;
-  p.splits = pl.splits;
-  p.tiles_per_split = pl.tiles_per_split;
-  p.out = a->out;
-  p.o_sb = a->o_sb; p.o_sm = a->o_sm; p.o_sh = a->o_sh;
-  p.out_f32 = a->out_f32;
-  p.lse = a->lse;
-  p.lse_sb = a->lse_sb; p.lse_sm = a->lse_sm; p.lse_sh = a->lse_sh;
-  p.aux = a->aux_lse;
-  p.aux_sb = a->aux_sb; p.aux_sm = a->aux_sm; p.aux_sh = a->aux_sh;
-  p.weight = a->weight;
-  p.w_sb = a->w_sb; p.w_sm = a->w_sm; p.w_sh = a->w_sh;
-  p.err = a->status;
-  p.trace = g_trace;
-  if (pl.splits > 1) {
-    const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
-    const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);
-    p.part_o = static_cast<float*>(a->workspace);
-    p.part_lse = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + ((o + 255) & ~size_t(255)));
-  }
+  fill_params(a, pl, pl.splits > 1, p);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Short key ranges take the split-P PV product (see attn_mma.cu); long ones
-  // average the bf16 rounding of P away.  Bit 4 of `kernel` forces it.
-  const bool precise = (a->kernel & 16) || a->num_keys <= kPreciseMaxKeys;
-  int rc = pl.tc ? launch_attn_tc(p, a->dtype, a->head_dim, st)
-                 : launch_attn_mma(p, a->dtype, a->head_dim, precise, st);
+  int rc = launch_attention(a, pl, p, st);
   if (rc != TV_OK) return rc;
   if (pl.splits > 1) rc = launch_split_combine(p, a->dtype, a->head_dim, st);
   return rc;
+}
+
+int tv_verify_attn_sharded_workspace_size(const tv_attn_args* a, size_t* bytes) {
+  if (!bytes) return TV_ERR_NULL;
+  *bytes = 0;
+  const int v = validate(a);
+  if (v != TV_OK) return v;
+  if (a->batch == 0 || a->rows == 0) return TV_OK;
+  *bytes = partial_bytes(a, plan(a).splits);
+  return TV_OK;
+}
+
+int tv_verify_attn_sharded(const tv_attn_args* a, int32_t world, int32_t rank, const void* const* bases,
+                           void* stream) {
+  const int v = validate(a);
+  if (v != TV_OK) return v;
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world) return TV_ERR_SHAPE;
+  if (!bases) return TV_ERR_NULL;
+  for (int r = 0; r < world; ++r) {
+    if (!bases[r]) return TV_ERR_NULL;
+    if (!aligned16(bases[r])) return TV_ERR_ALIGN;
+  }
+  if (a->batch == 0 || a->rows == 0) return TV_OK;
+  const Plan pl = plan(a);
+  const size_t need = partial_bytes(a, pl.splits);
+  if (!a->workspace || a->workspace_bytes < need) return TV_ERR_WORKSPACE;
+  if (!aligned16(a->workspace)) return TV_ERR_ALIGN;
+  AttnParams p;
+  fill_params(a, pl, true, p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rc = launch_attention(a, pl, p, st);
+  if (rc != TV_OK) return rc;
+  return launch_sharded_combine(p, a->dtype, a->head_dim, world, rank, bases, st);
 }
 
 int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim, const float* parts_o, int64_t part_stride_o,

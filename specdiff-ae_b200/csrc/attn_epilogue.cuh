@@ -43,4 +43,56 @@ __device__ __forceinline__ float* part_lse_row(const AttnParams& p, int split, i
   return p.part_lse + ((int64_t)split * p.B * p.Hkv + bh) * p.R + r;
 }
 
+// Log-sum-exp combine of the p.splits split partials of kernel row (bh, r):
+// this thread's four head-dim values 4q .. 4q+3 (normalised) and the row's
+// LSE.  Partials are read up to 8 splits at a time (all loads of a block in
+// flight together; they are usually still in L2) and folded with a running
+// max, so the row needs one pass.
+template <int D>
+__device__ __forceinline__ void combine_split_row(const AttnParams& p, int bh, int r, int q, float4& o,
+                                                  float& lse) {
+  constexpr int BLK = 8;
+  float mx = -INFINITY, wsum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < p.splits; s0 += BLK) {
+    float l[BLK];
+    float4 v[BLK];
+#pragma unroll
+    for (int j = 0; j < BLK; ++j) {
+      const int s = s0 + j;
+      if (s < p.splits) {
+        l[j] = *part_lse_row(p, s, bh, r);
+        v[j] = *reinterpret_cast<const float4*>(part_o_row(p, s, bh, r, D) + 4 * q);
+      } else {
+        l[j] = -INFINITY;
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float bm = l[0];
+#pragma unroll
+    for (int j = 1; j < BLK; ++j) bm = fmaxf(bm, l[j]);
+    const float nm = fmaxf(mx, bm);
+    if (nm == -INFINITY) continue;
+    const float sc = mx == -INFINITY ? 0.f : expf(mx - nm);
+    acc.x *= sc;
+    acc.y *= sc;
+    acc.z *= sc;
+    acc.w *= sc;
+    wsum *= sc;
+#pragma unroll
+    for (int j = 0; j < BLK; ++j) {
+      const float w = l[j] == -INFINITY ? 0.f : expf(l[j] - nm);
+      wsum += w;
+      acc.x += w * v[j].x;
+      acc.y += w * v[j].y;
+      acc.z += w * v[j].z;
+      acc.w += w * v[j].w;
+    }
+    mx = nm;
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  lse = wsum > 0.f ? mx + logf(wsum) : -INFINITY;
+  o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
 }  // namespace tv

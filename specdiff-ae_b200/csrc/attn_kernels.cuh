@@ -23,4 +23,12 @@ int tc_row_blocks(int R);   // CTAs per (batch, KV head); pairs above 128 rows
 // Log-sum-exp merge of split partials into the final outputs of AttnParams.
 int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st);
 
+// Sequence-sharded step, after the attention kernel left this rank's split
+// partials in p.part_o / p.part_lse: combine them, push the result into every
+// peer's exchange buffer, wait for the peers' and merge all ranks' partials
+// into the final outputs of AttnParams (same on every rank).
+constexpr int kMaxPeers = 8;
+int launch_sharded_combine(const AttnParams& p, int dtype, int D, int world, int rank, const void* const* bases,
+                           cudaStream_t st);
+
 }  // namespace tv

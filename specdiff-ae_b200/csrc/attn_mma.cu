@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
   const float lse0 = l0 > 0.f ? (mx0 + __log2f(l0)) * kLn2 : -INFINITY;
   const float lse1 = l1 > 0.f ? (mx1 + __log2f(l1)) * kLn2 : -INFINITY;
 
-  if (p.splits == 1) {
+  if (!p.part_o) {
     if (r0 < p.R) {
       int m, h;
       row_coords(p, hk, r0, m, h);

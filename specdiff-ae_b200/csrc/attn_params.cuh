@@ -35,7 +35,9 @@ struct AttnParams {
   int64_t aux_sb, aux_sm, aux_sh;
   void* weight;
   int64_t w_sb, w_sm, w_sh;
-  // split partials: [splits][B*Hkv][R][D] and [splits][B*Hkv][R]
+  // split partials: [splits][B*Hkv][R][D] and [splits][B*Hkv][R].  When set
+  // (always with splits > 1; also with one split for the sharded path), the
+  // kernels write normalised partials here instead of the final outputs.
   float* part_o;
   float* part_lse;
   int* err;                // optional device status word (nonzero = a wait gave up)

@@ -759,7 +759,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int ch = par;                           // this warp writes head-dim columns ch*64 .. +63
     int mm = 0, hh = 0;
     if (valid) row_coords(p, hk, r, mm, hh);
-    float* prow = valid && p.splits > 1 ? part_o_row(p, split, bh, r, HD) : nullptr;
+    float* prow = valid && p.part_o ? part_o_row(p, split, bh, r, HD) : nullptr;
     const int d0 = ch * (HD / 2);
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {

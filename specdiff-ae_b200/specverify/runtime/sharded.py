@@ -10,14 +10,17 @@ partials are exchanged and every rank merges them in rank order:
 
     O = sum_r e^{lse_r - L} O_r / sum_r e^{lse_r - L},   L = max_r lse_r
 
-Default exchange: NVLink peer memory.  Each rank writes its partial into a
-buffer mapped into every rank (torch symmetric memory) and one kernel,
-``tv_peer_merge``, publishes it, waits for every peer's and merges all
-partials straight from the peers' memory -- no collective launch.  Fallback
-(and the host-testable form): ONE NCCL ``all_gather`` of the packed partials
-and ``tv_merge_partials``.  Both are order-fixed, so every rank gets
-bit-identical results (the next layer's replicated projections need that).
-An all-reduce formulation would need a max-reduce first: two collectives.
+Default exchange: NVLink peer memory, one C call per rank
+(``tv_verify_attn_sharded``).  After the attention kernel one kernel combines
+this rank's split partials, stores the result straight into every peer's
+exchange buffer (mapped into every rank through torch symmetric memory),
+raises a flag per row block on each peer, waits on its own buffer for the
+peers' row blocks and merges -- no collective launch, no remote reads, and
+no step-wide barrier.  Fallback (and the host-testable form): ONE NCCL
+``all_gather`` of the packed partials and ``tv_merge_partials``.  Both are
+order-fixed, so every rank gets bit-identical results (the next layer's
+replicated projections need that).  An all-reduce formulation would need a
+max-reduce first: two collectives.
 """
 
 from __future__ import annotations
@@ -29,7 +32,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _lib
-from .tree_attention import attention, pack_tree_mask
+from .tree_attention import attention, attn_args, pack_tree_mask
 
 
 def shard_bounds(total: int, world: int, rank: int, align: int = 1) -> Tuple[int, int]:
@@ -83,55 +86,41 @@ def merge_packed(gathered: torch.Tensor, part: PackedPartial, world: int, out_dt
 
 
 class PeerExchange:
-    """Partials exchanged through NVLink peer memory instead of a collective.
+    """This rank's exchange buffer for ``tv_verify_attn_sharded``, mapped into
+    every rank of ``group`` (torch symmetric memory): two slots of all ranks'
+    fp32 partials, per-row-block flags and the step count, zeroed once.
+    Successive steps alternate the slots inside the kernel, so the calls can
+    be captured into CUDA graphs and replayed any number of times."""
 
-    One buffer per rank, mapped into every rank (torch symmetric memory):
-    two partial slots (successive steps alternate), two flags and a step
-    counter.  A step writes this rank's partial into its slot, then
-    ``tv_peer_merge`` publishes it, waits for every peer's flag and merges
-    all ranks' partials straight from their memory.
-    """
-
-    def __init__(self, group, b, m, h, d, device):
+    def __init__(self, group, rows, d, device):
         import torch.distributed._symmetric_memory as symm
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.shape = (b, m, h, d)
-        self.rows = b * m * h
-        self.slot_floats = -(-(self.rows * d + self.rows) // 64) * 64       # 256-byte aligned slots
-        total = 2 * self.slot_floats + 64
-        self.buf = symm.empty(total, dtype=torch.float32, device=device)
-        self.buf.zero_()                                                     # flags and counter start at 0
+        lib = _lib.load()
+        nbytes = ctypes.c_int64(0)
+        _lib.check(lib.tv_sharded_exchange_bytes(self.world, rows, d, ctypes.byref(nbytes)),
+                   "tv_sharded_exchange_bytes")
+        self.buf = symm.empty(-(-nbytes.value // 4), dtype=torch.int32, device=device)
+        self.buf.zero_()
         torch.cuda.synchronize(device)
         self.handle = symm.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
-        ptrs = list(self.handle.buffer_ptrs)
-        self.bases = (ctypes.c_void_p * self.world)(*ptrs)
-        flag_floats = 2 * self.slot_floats
-        self.counter = self.buf[flag_floats + 4:flag_floats + 5].view(torch.int32)
-        self.flag_offset = flag_floats * 4
-        self.step = 0
-        dist.barrier(group)    # every rank's zeroed flags are in place before anyone waits on them
+        self.bases = (ctypes.c_void_p * self.world)(*list(self.handle.buffer_ptrs))
+        self._ws = None
+        dist.barrier(group)    # every rank's zeroed flags are in place before anyone writes to them
 
-    def slot(self):
-        s = self.step & 1
-        self.step += 1
-        return s
-
-    def views(self, s):
-        b, m, h, d = self.shape
-        base = s * self.slot_floats
-        o = self.buf[base:base + self.rows * d].view(b, m, h, d)
-        lse = self.buf[base + self.rows * d:base + self.rows * d + self.rows].view(b, m, h)
-        return o, lse
-
-    def merge(self, s, out, out_lse, status=None):
+    def run(self, a, device):
+        """``tv_verify_attn_sharded`` of the request ``a`` (see ``attn_args``)."""
         lib = _lib.load()
-        dev = out.device
-        stream = _lib.stream_ptr(dev)
-        _lib.check(lib.tv_peer_merge(self.world, self.rank, self.bases, self.slot_floats * 4, s, self.flag_offset,
-                                     self.counter.data_ptr(), self.rows, self.shape[3], _lib.dtype_code(out.dtype),
-                                     out.data_ptr(), _lib.ptr(out_lse), _lib.ptr(status), stream), "tv_peer_merge")
+        need = ctypes.c_size_t(0)
+        _lib.check(lib.tv_verify_attn_sharded_workspace_size(ctypes.byref(a), ctypes.byref(need)),
+                   "tv_verify_attn_sharded_workspace_size")
+        if self._ws is None or self._ws.numel() < need.value:
+            self._ws = torch.empty(max(need.value, 256), dtype=torch.uint8, device=device)
+        a.workspace = self._ws.data_ptr()
+        a.workspace_bytes = self._ws.numel()
+        _lib.check(lib.tv_verify_attn_sharded(ctypes.byref(a), self.world, self.rank, self.bases,
+                                              _lib.stream_ptr(device)), "tv_verify_attn_sharded")
 
 
 class SequenceShardedVerify:
@@ -164,7 +153,7 @@ class SequenceShardedVerify:
         key = (b, m, h, d, str(device))
         if key not in self._peer:
             try:
-                self._peer[key] = PeerExchange(self.group, b, m, h, d, device)
+                self._peer[key] = PeerExchange(self.group, b * m * h, d, device)
             except Exception:
                 if self.exchange == "peer":
                     raise
@@ -198,13 +187,11 @@ class SequenceShardedVerify:
             mlen = m
         peer = self._peer_exchange(b, m, h, d, q.device)
         if peer is not None:
-            s = peer.slot()
-            o_part, l_part = peer.views(s)
-            attention(q, k_shard, v_shard, num_keys=shard_len, page_table=page_table, mask_bits=bits,
-                      mask_len=mlen, out=o_part, lse=l_part, num_splits=num_splits)
             out = torch.empty((b, m, h, d), dtype=out_dtype or q.dtype, device=q.device)
             lse = torch.empty((b, m, h), dtype=torch.float32, device=q.device) if return_lse else None
-            peer.merge(s, out, lse)
+            a, out = attn_args(q, k_shard, v_shard, num_keys=shard_len, page_table=page_table, mask_bits=bits,
+                               mask_len=mlen, out=out, lse=lse, num_splits=num_splits)
+            peer.run(a, q.device)
             return (out, lse) if return_lse else out
         part, gathered = self.buffers(b, m, h, d, q.device)
         self.partial_fn(part, q, k_shard, v_shard, shard_len, bits, mlen, page_table, num_splits)

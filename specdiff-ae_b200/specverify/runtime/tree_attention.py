@@ -142,6 +142,28 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     receives a nonzero code if a kernel had to abandon a bounded wait.
     Returns ``out``.
     """
+    a, out = attn_args(q, k, v, num_keys=num_keys, kv_lens=kv_lens, page_table=page_table, mask_bits=mask_bits,
+                       mask_len=mask_len, out=out, out_f32=out_f32, lse=lse, lse_strides=lse_strides,
+                       aux_lse=aux_lse, aux_strides=aux_strides, weight=weight, weight_strides=weight_strides,
+                       scale=scale, num_splits=num_splits, kernel=kernel, status=status)
+    lib = _lib.load()
+    need = ctypes.c_size_t(0)
+    _lib.check(lib.tv_attn_workspace_size(ctypes.byref(a), ctypes.byref(need)), "tv_attn_workspace_size")
+    ws = None
+    if need.value:
+        ws = torch.empty(need.value, dtype=torch.uint8, device=out.device)
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = need.value
+    _lib.check(lib.tv_verify_attn(ctypes.byref(a), _lib.stream_ptr(out.device)), "tv_verify_attn")
+    return out
+
+
+def attn_args(q, k, v, *, num_keys=None, kv_lens=None, page_table=None, mask_bits=None, mask_len=0, out=None,
+              out_f32=False, lse=None, lse_strides=None, aux_lse=None, aux_strides=None, weight=None,
+              weight_strides=None, scale=None, num_splits=0, kernel=0, status=None):
+    """The checked ``tv_attn_args`` of an :func:`attention` request (no
+    workspace set) and its output tensor (allocated when ``out`` is None).
+    The tensors must stay alive while the struct is used."""
     dev = _lib.require_cuda(q, k, v, page_table, kv_lens, mask_bits, out, lse, aux_lse, weight)
     if q.dim() != 4 or q.stride(3) != 1:
         raise _lib.SpecVerifyError(-3, f"q must be [B, M, H, D] with unit stride on D, got {tuple(q.shape)}")
@@ -221,16 +243,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         if status.dtype != torch.int32 or not status.is_cuda:
             raise _lib.SpecVerifyError(-2, "status must be a CUDA int32 tensor")
         a.status = status.data_ptr()
-    lib = _lib.load()
-    need = ctypes.c_size_t(0)
-    _lib.check(lib.tv_attn_workspace_size(ctypes.byref(a), ctypes.byref(need)), "tv_attn_workspace_size")
-    ws = None
-    if need.value:
-        ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
-        a.workspace = ws.data_ptr()
-        a.workspace_bytes = need.value
-    _lib.check(lib.tv_verify_attn(ctypes.byref(a), _lib.stream_ptr(dev)), "tv_verify_attn")
-    return out
+    return a, out
 
 
 def prefix_attention_forward(query_states, key_states, value_states, bsz, q_len, num_heads, hidden_dim):

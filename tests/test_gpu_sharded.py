@@ -88,3 +88,73 @@ def test_sharded_exchanges_match_single_gpu(tmp_path):
         torch.testing.assert_close(first_l, ref_lse, rtol=1e-5, atol=1e-5)
     # both exchanges merge the same partials with the same algebra
     torch.testing.assert_close(r[0]["peer"][0][0].float(), r[0]["nccl"][0][0].float(), rtol=0, atol=2e-3)
+
+
+def _one_gpu_request(prefix_len, seed):
+    sys.path.insert(0, str(ROOT / "specdiff-ae_b200"))
+    from specverify import workloads as wl
+    from specverify.runtime import pack_tree_mask
+    w = wl.paged_verify(prefix_len=prefix_len, nodes=64, per_depth=8, seed=seed, device=torch.device("cuda", 0))
+    return w, pack_tree_mask(w.tree.keep.cuda())
+
+
+def _sharded_call(w, bits, bases, world, rank, status=None, num_splits=0):
+    import ctypes
+    from specverify import _lib
+    from specverify.runtime.tree_attention import attn_args
+    out = torch.empty_like(w.q)
+    lse = torch.empty(w.q.shape[:3], device="cuda")
+    a, _ = attn_args(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
+                     mask_len=w.tree.rows, out=out, lse=lse, status=status, num_splits=num_splits)
+    lib = _lib.load()
+    need = ctypes.c_size_t(0)
+    _lib.check(lib.tv_verify_attn_sharded_workspace_size(ctypes.byref(a), ctypes.byref(need)), "workspace")
+    ws = torch.empty(need.value, dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes = ws.data_ptr(), need.value
+    arr = (ctypes.c_void_p * world)(*bases)
+    _lib.check(lib.tv_verify_attn_sharded(ctypes.byref(a), world, rank, arr, _lib.stream_ptr(out.device)),
+               "tv_verify_attn_sharded")
+    torch.cuda.synchronize()
+    return out, lse
+
+
+def _exchange_buffer(world, rows, d):
+    import ctypes
+    from specverify import _lib
+    n = ctypes.c_int64(0)
+    _lib.check(_lib.load().tv_sharded_exchange_bytes(world, rows, d, ctypes.byref(n)), "exchange bytes")
+    return torch.zeros(n.value, dtype=torch.uint8, device="cuda")
+
+
+@pytest.mark.skipif(not cuda_ok(), reason="needs CUDA")
+@pytest.mark.parametrize("num_splits", [0, 1])             # planned splits; one split (partial, not final)
+@pytest.mark.parametrize("prefix_len", [1024, 8192])       # warp-MMA kernel, tensor-memory kernel
+def test_sharded_entry_one_rank_equals_verify_attn(prefix_len, num_splits):
+    """world = 1: the fused combine + exchange + merge kernel reduces to the
+    split combine; five steps walk both slots and the step counter."""
+    from specverify.runtime import attention
+    w, bits = _one_gpu_request(prefix_len, seed=5)
+    b, m, h, d = w.q.shape
+    ref = torch.empty_like(w.q)
+    ref_lse = torch.empty(w.q.shape[:3], device="cuda")
+    attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
+              mask_len=m, out=ref, lse=ref_lse, num_splits=num_splits)
+    buf = _exchange_buffer(1, b * m * h, d)
+    for step in range(5):
+        out, lse = _sharded_call(w, bits, [buf.data_ptr()], 1, 0, num_splits=num_splits)
+        assert torch.equal(out, ref) and torch.equal(lse, ref_lse), step
+
+
+@pytest.mark.skipif(not cuda_ok(), reason="needs CUDA")
+def test_sharded_entry_gives_up_on_a_silent_peer():
+    """Two ranks, but the 'peer' buffer is local memory that no rank ever
+    flags: every wait runs out (2 s), the status word reads 8 and the
+    outputs are NaN instead of a silent one-rank result."""
+    w, bits = _one_gpu_request(1024, seed=6)
+    b, m, h, d = w.q.shape
+    mine = _exchange_buffer(2, b * m * h, d)
+    silent = _exchange_buffer(2, b * m * h, d)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out, lse = _sharded_call(w, bits, [mine.data_ptr(), silent.data_ptr()], 2, 0, status=status)
+    assert int(status.item()) == 8
+    assert torch.isnan(out.float()).all() and torch.isnan(lse).all()
