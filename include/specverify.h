@@ -137,7 +137,10 @@ typedef struct tv_attn_args {
   int32_t kernel;                /* bits 0-3: 0 auto, 1 warp-MMA, 2 tcgen05;
                                     bit 4 (16): softmax weights as a hi+lo
                                     16-bit pair in the PV product (automatic
-                                    for num_keys <= 4096)                   */
+                                    for num_keys <= 4096);
+                                    tv_verify_attn_sharded only: bit 5 (32)
+                                    owner exchange, bit 6 (64) push to every
+                                    peer (default: owner from 3 ranks on)  */
   void* workspace;
   size_t workspace_bytes;
   int32_t* status;               /* optional device word, zeroed by the caller;
@@ -187,11 +190,15 @@ int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
  * aux_lse / weight receive the MERGED result over all ranks' shards, and
  * args->workspace holds this rank's split partials
  * (tv_verify_attn_sharded_workspace_size bytes).  It launches the attention
- * kernel, then one kernel that combines this rank's split partials, stores
- * them into every peer's buffer, publishes per-row-block flags with a
- * system-scope release, waits on its own buffer for the peers' (bounded:
- * 2 s, then *args->status = 8 and NaN rows) and merges all ranks' partials by
- * log-sum-exp in rank order: every rank gets bit-identical outputs.
+ * kernel, then one kernel that combines this rank's split partials and
+ * exchanges them over NVLink with per-row-block flags (system-scope
+ * release / acquire, waits bounded: 2 s, then *args->status = 8 and NaN
+ * rows).  Push mode: the partial goes into every peer's buffer and every rank
+ * merges all partials.  Owner mode: each row block's partials go to the rank
+ * that owns it, which merges them and stores the final fp32 rows into every
+ * other rank's buffer (about 2 (W-1)/W partials of NVLink traffic per rank
+ * instead of W-1).  Merges run by log-sum-exp in rank order: every rank gets
+ * bit-identical outputs.  args->kernel bits 5 / 6 pick the mode.
  * bases[r] = rank r's exchange buffer as mapped in this process (world <= 8).
  * Every rank must make the same sequence of calls with the same shapes;
  * successive calls alternate the buffer's two slots by themselves. */

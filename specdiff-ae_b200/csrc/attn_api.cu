@@ -347,7 +347,9 @@ int tv_verify_attn_sharded(const tv_attn_args* a, int32_t world, int32_t rank, c
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int rc = launch_attention(a, pl, p, st);
   if (rc != TV_OK) return rc;
-  return launch_sharded_combine(p, a->dtype, a->head_dim, world, rank, bases, st);
+  // Exchange mode: bit 5 owner, bit 6 push to all, else owner from 3 ranks on.
+  const bool owned = (a->kernel & 32) ? true : (a->kernel & 64) ? false : world >= 3;
+  return launch_sharded_combine(p, a->dtype, a->head_dim, world, rank, bases, owned, st);
 }
 
 int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim, const float* parts_o, int64_t part_stride_o,

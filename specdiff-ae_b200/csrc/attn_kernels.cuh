@@ -24,11 +24,12 @@ int tc_row_blocks(int R);   // CTAs per (batch, KV head); pairs above 128 rows
 int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st);
 
 // Sequence-sharded step, after the attention kernel left this rank's split
-// partials in p.part_o / p.part_lse: combine them, push the result into every
-// peer's exchange buffer, wait for the peers' and merge all ranks' partials
-// into the final outputs of AttnParams (same on every rank).
+// partials in p.part_o / p.part_lse: combine them, exchange them with the
+// peers over NVLink (pushed to every peer, or -- `owned` -- to the rank that
+// owns each row block, which merges and hands the final rows back) and write
+// the merged final outputs of AttnParams (same on every rank).
 constexpr int kMaxPeers = 8;
 int launch_sharded_combine(const AttnParams& p, int dtype, int D, int world, int rank, const void* const* bases,
-                           cudaStream_t st);
+                           bool owned, cudaStream_t st);
 
 }  // namespace tv

@@ -132,11 +132,21 @@ class SequenceShardedVerify:
     exchange can be exercised with CPU ``gloo`` ranks.
     """
 
+    _PEER_MODES = {"auto": 0, "owner": 32, "push": 64}
+
     def __init__(self, group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
-                 exchange: str = "auto"):
+                 exchange: str = "auto", peer_mode: str = "auto"):
         """``exchange``: ``"peer"`` (NVLink peer memory, kernels only),
         ``"nccl"`` (one all_gather), or ``"auto"`` (peer when the default
-        CUDA partial and merge are used and peer mapping succeeds)."""
+        CUDA partial and merge are used and peer mapping succeeds).
+        ``peer_mode`` (peer exchange): ``"push"`` (every rank's partial to
+        every peer, one hop), ``"owner"`` (each row block's partials to the
+        rank owning it, which hands the final rows back: two hops, less
+        NVLink traffic from three ranks on) or ``"auto"`` (owner from three
+        ranks on)."""
+        if peer_mode not in self._PEER_MODES:
+            raise ValueError(f"peer_mode must be one of {sorted(self._PEER_MODES)}")
+        self.peer_bits = self._PEER_MODES[peer_mode]
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -190,7 +200,7 @@ class SequenceShardedVerify:
             out = torch.empty((b, m, h, d), dtype=out_dtype or q.dtype, device=q.device)
             lse = torch.empty((b, m, h), dtype=torch.float32, device=q.device) if return_lse else None
             a, out = attn_args(q, k_shard, v_shard, num_keys=shard_len, page_table=page_table, mask_bits=bits,
-                               mask_len=mlen, out=out, lse=lse, num_splits=num_splits)
+                               mask_len=mlen, out=out, lse=lse, num_splits=num_splits, kernel=self.peer_bits)
             peer.run(a, q.device)
             return (out, lse) if return_lse else out
         part, gathered = self.buffers(b, m, h, d, q.device)

@@ -57,8 +57,9 @@ def _rank_main(rank, world, port, out_dir):
         attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
                   mask_len=m, out=ref, lse=ref_lse)
         res = {"ref": ref.cpu(), "ref_lse": ref_lse.cpu()}
-        for mode in ("peer", "nccl"):
-            ver = sh.SequenceShardedVerify(exchange=mode)
+        for mode in ("peer", "owner", "nccl"):
+            ver = sh.SequenceShardedVerify(exchange="nccl" if mode == "nccl" else "peer",
+                                           peer_mode="owner" if mode == "owner" else "push")
             outs = [ver(w.q, w.k_pool, w.v_pool, shard_len, bits if last else None, page_table=tbl, return_lse=True)
                     for _ in range(5)]
             torch.cuda.synchronize()
@@ -77,7 +78,7 @@ def test_sharded_exchanges_match_single_gpu(tmp_path):
                        start_method="spawn")
     r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(world)]
     ref, ref_lse = r[0]["ref"].float(), r[0]["ref_lse"]
-    for mode in ("peer", "nccl"):
+    for mode in ("peer", "owner", "nccl"):
         first_o, first_l = r[0][mode][0]
         for rank in range(world):
             for o, l in r[rank][mode]:
@@ -86,6 +87,8 @@ def test_sharded_exchanges_match_single_gpu(tmp_path):
         # two merges of fp32 partials vs the kernel's own split merge: bf16 rounding apart
         torch.testing.assert_close(first_o.float(), ref, rtol=2e-2, atol=2e-3)
         torch.testing.assert_close(first_l, ref_lse, rtol=1e-5, atol=1e-5)
+    # both NVLink modes run the same merge in rank order: identical bits
+    assert torch.equal(r[0]["peer"][0][0], r[0]["owner"][0][0]) and torch.equal(r[0]["peer"][0][1], r[0]["owner"][0][1])
     # both exchanges merge the same partials with the same algebra
     torch.testing.assert_close(r[0]["peer"][0][0].float(), r[0]["nccl"][0][0].float(), rtol=0, atol=2e-3)
 
@@ -98,14 +101,14 @@ def _one_gpu_request(prefix_len, seed):
     return w, pack_tree_mask(w.tree.keep.cuda())
 
 
-def _sharded_call(w, bits, bases, world, rank, status=None, num_splits=0):
+def _sharded_call(w, bits, bases, world, rank, status=None, num_splits=0, kernel=0):
     import ctypes
     from specverify import _lib
     from specverify.runtime.tree_attention import attn_args
     out = torch.empty_like(w.q)
     lse = torch.empty(w.q.shape[:3], device="cuda")
     a, _ = attn_args(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
-                     mask_len=w.tree.rows, out=out, lse=lse, status=status, num_splits=num_splits)
+                     mask_len=w.tree.rows, out=out, lse=lse, status=status, num_splits=num_splits, kernel=kernel)
     lib = _lib.load()
     need = ctypes.c_size_t(0)
     _lib.check(lib.tv_verify_attn_sharded_workspace_size(ctypes.byref(a), ctypes.byref(need)), "workspace")
@@ -146,15 +149,18 @@ def test_sharded_entry_one_rank_equals_verify_attn(prefix_len, num_splits):
 
 
 @pytest.mark.skipif(not cuda_ok(), reason="needs CUDA")
-def test_sharded_entry_gives_up_on_a_silent_peer():
+@pytest.mark.parametrize("mode", [32, 64])                  # owner exchange, push to all
+def test_sharded_entry_gives_up_on_a_silent_peer(mode):
     """Two ranks, but the 'peer' buffer is local memory that no rank ever
     flags: every wait runs out (2 s), the status word reads 8 and the
-    outputs are NaN instead of a silent one-rank result."""
+    outputs are NaN instead of a silent one-rank result.  In owner mode
+    rank 0 owns half the row blocks (waits for the peer's partials) and
+    waits for the peer's final rows on the other half."""
     w, bits = _one_gpu_request(1024, seed=6)
     b, m, h, d = w.q.shape
     mine = _exchange_buffer(2, b * m * h, d)
     silent = _exchange_buffer(2, b * m * h, d)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    out, lse = _sharded_call(w, bits, [mine.data_ptr(), silent.data_ptr()], 2, 0, status=status)
+    out, lse = _sharded_call(w, bits, [mine.data_ptr(), silent.data_ptr()], 2, 0, status=status, kernel=mode)
     assert int(status.item()) == 8
     assert torch.isnan(out.float()).all() and torch.isnan(lse).all()
