@@ -139,8 +139,9 @@ typedef struct tv_attn_args {
                                     16-bit pair in the PV product (automatic
                                     for num_keys <= 4096);
                                     tv_verify_attn_sharded only: bit 5 (32)
-                                    owner exchange, bit 6 (64) push to every
-                                    peer (default: owner from 3 ranks on)  */
+                                    owner exchange instead of the default
+                                    push to every peer (bit 6 (64) asks for
+                                    push explicitly)                       */
   void* workspace;
   size_t workspace_bytes;
   int32_t* status;               /* optional device word, zeroed by the caller;
@@ -197,8 +198,9 @@ int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
  * merges all partials.  Owner mode: each row block's partials go to the rank
  * that owns it, which merges them and stores the final fp32 rows into every
  * other rank's buffer (about 2 (W-1)/W partials of NVLink traffic per rank
- * instead of W-1).  Merges run by log-sum-exp in rank order: every rank gets
- * bit-identical outputs.  args->kernel bits 5 / 6 pick the mode.
+ * instead of W-1, but a second flag hand-off; measured slower at two
+ * ranks).  Merges run by log-sum-exp in rank order: every rank gets
+ * bit-identical outputs.  args->kernel bit 5 selects owner mode.
  * bases[r] = rank r's exchange buffer as mapped in this process (world <= 8).
  * Every rank must make the same sequence of calls with the same shapes;
  * successive calls alternate the buffer's two slots by themselves. */

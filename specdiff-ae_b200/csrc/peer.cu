@@ -17,13 +17,13 @@
 // Step e (1, 2, ...) uses slot e & 1.  Each block takes row blocks of RPB rows
 // and combines this rank's split partials of those rows (local memory).  Two
 // exchange modes:
-//  * push to all (default for W <= 2): the block stores its rows into every
+//  * push to all (default): the block stores its rows into every
 //    peer's slot region for this rank (posted NVLink writes), publishes
 //    flags[slot][rank][row block] = e on each peer with a system-scope
 //    release, waits -- on its own, local flags -- until every peer has
 //    published the same row block, and merges all W partials by log-sum-exp
 //    in rank order.  One NVLink hop; (W - 1) x the partial leaves each rank.
-//  * owner (default for W >= 3): row block rb belongs to rank rb * W / nrb.
+//  * owner (on request): row block rb belongs to rank rb * W / nrb.
 //    Every other rank pushes its partial rows of rb to the owner only; the
 //    owner merges them in rank order and pushes the final fp32 rows to every
 //    other rank, which convert them exactly as the owner does.  Two hops, but
