@@ -139,9 +139,9 @@ typedef struct tv_attn_args {
                                     16-bit pair in the PV product (automatic
                                     for num_keys <= 4096);
                                     tv_verify_attn_sharded only: bit 5 (32)
-                                    owner exchange instead of the default
-                                    push to every peer (bit 6 (64) asks for
-                                    push explicitly)                       */
+                                    owner exchange, bit 6 (64) push to every
+                                    peer (default: push below 4 ranks,
+                                    owner from 4 on)                       */
   void* workspace;
   size_t workspace_bytes;
   int32_t* status;               /* optional device word, zeroed by the caller;
@@ -192,15 +192,17 @@ int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
  * args->workspace holds this rank's split partials
  * (tv_verify_attn_sharded_workspace_size bytes).  It launches the attention
  * kernel, then one kernel that combines this rank's split partials and
- * exchanges them over NVLink with per-row-block flags (system-scope
- * release / acquire, waits bounded: 2 s, then *args->status = 8 and NaN
- * rows).  Push mode: the partial goes into every peer's buffer and every rank
+ * exchanges them over NVLink as 8-byte words that carry the value (fp32 bits,
+ * low half) and the step number (high half): an aligned 64-bit store is
+ * single-copy atomic, so the reader polls the data itself -- no flags, no
+ * fences.  Waits are bounded: 2 s, then *args->status = 8 and NaN rows.
+ * Push mode: the partial goes into every peer's buffer and every rank
  * merges all partials.  Owner mode: each row block's partials go to the rank
- * that owns it, which merges them and stores the final fp32 rows into every
- * other rank's buffer (about 2 (W-1)/W partials of NVLink traffic per rank
- * instead of W-1, but a second flag hand-off; measured slower at two
- * ranks).  Merges run by log-sum-exp in rank order: every rank gets
- * bit-identical outputs.  args->kernel bit 5 selects owner mode.
+ * that owns it, which merges them and stores the final rows into every other
+ * rank's buffer (about 4 (W-1)/W partials of NVLink bytes per rank instead of
+ * 2 (W-1), for a second hop).  Merges run by log-sum-exp in rank order:
+ * every rank gets bit-identical outputs.  args->kernel bits 5 / 6 pick the
+ * mode (default: push below 4 ranks, owner from 4 on).
  * bases[r] = rank r's exchange buffer as mapped in this process (world <= 8).
  * Every rank must make the same sequence of calls with the same shapes;
  * successive calls alternate the buffer's two slots by themselves. */

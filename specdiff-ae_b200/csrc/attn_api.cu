@@ -347,9 +347,9 @@ int tv_verify_attn_sharded(const tv_attn_args* a, int32_t world, int32_t rank, c
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int rc = launch_attention(a, pl, p, st);
   if (rc != TV_OK) return rc;
-  // Exchange mode: bit 5 owner; otherwise push to all (measured faster at
-  // two ranks: each owner hop costs about as much as the whole push).
-  const bool owned = (a->kernel & 32) != 0;
+  // Exchange mode: bit 5 owner, bit 6 push to all; by default push below four
+  // ranks, owner from four on (push sends 2 (W-1) partials per rank).
+  const bool owned = (a->kernel & 32) ? true : (a->kernel & 64) ? false : world >= 4;
   return launch_sharded_combine(p, a->dtype, a->head_dim, world, rank, bases, owned, st);
 }
 

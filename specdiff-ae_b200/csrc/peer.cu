@@ -2,43 +2,47 @@
 // memory, fused with the combine of this rank's split-KV partials and the
 // final merge (one kernel after the attention kernel, one process per GPU).
 //
+// Every value crosses NVLink as an 8-byte word: the fp32 bits in the low
+// half, the step number e in the high half.  An aligned 64-bit store is
+// single-copy atomic, so a reader that sees step >= e in a word also sees
+// that step's value: no flags, no fences.  (System-scope fence + flag pairs,
+// one per block, measured ~15 us per step on B200 even with no peer to wait
+// for; the words double the bytes instead, ~1 us per MB at NVLink rates.)
+//
 // Each rank owns one exchange buffer, mapped into every rank's address space
 // (rows = B * H * M query rows, in the attention kernel's row order
 // (b, kv head, node, group member); D = head_dim; W = world size):
-//   slot s (s = 0, 1) at s * slot_bytes:
-//     O   [W][rows][D] fp32        -- rank r's partial at r * rows * D
-//     LSE [W][rows] fp32
-//     final O [rows][D] fp32, final LSE [rows]   (owner mode)
-//   flags at flags_off: int32 [2][W][row blocks]   "partial arrived"
-//         at fin_flags_off: int32 [2][row blocks]  "final rows arrived"
-//   then two int32 words: [steps completed, blocks finished this step]
+//   slot s (s = 0, 1) at s * slot_bytes, all 8-byte words:
+//     O   [W][rows][D]      -- rank r's partial at r * rows * D
+//     LSE [W][rows]
+//     final O [rows][D], final LSE [rows]   (owner mode)
+//   then int32 step counts, one per block of the kernel's grid
 // all zero before the first step.
 //
 // Step e (1, 2, ...) uses slot e & 1.  Each block takes row blocks of RPB rows
 // and combines this rank's split partials of those rows (local memory).  Two
 // exchange modes:
-//  * push to all (default): the block stores its rows into every
-//    peer's slot region for this rank (posted NVLink writes), publishes
-//    flags[slot][rank][row block] = e on each peer with a system-scope
-//    release, waits -- on its own, local flags -- until every peer has
-//    published the same row block, and merges all W partials by log-sum-exp
-//    in rank order.  One NVLink hop; (W - 1) x the partial leaves each rank.
-//  * owner (on request): row block rb belongs to rank rb * W / nrb.
-//    Every other rank pushes its partial rows of rb to the owner only; the
-//    owner merges them in rank order and pushes the final fp32 rows to every
-//    other rank, which convert them exactly as the owner does.  Two hops, but
-//    about 2 x (W - 1) / W of one partial leaves each rank instead of W - 1.
-// Either way every rank computes bit-identical outputs and no block waits on
-// more than the row block it is working on.
+//  * push to all (default below 4 ranks): the block stores its rows into
+//    every peer's slot region for this rank, then waits on its own buffer
+//    until every peer's words of the same rows carry step e, and merges all
+//    W partials by log-sum-exp in rank order.  One hop; 2 (W - 1) x the
+//    fp32 partial leaves each rank.
+//  * owner (default from 4 ranks on): row block rb belongs to rank
+//    rb * W / nrb.  The other ranks push their partial rows of rb to the owner
+//    only; the owner merges them in rank order and pushes the final fp32 rows
+//    to every other rank, which convert them exactly as the owner does.  Two
+//    hops, but about 4 (W - 1) / W partials leave each rank instead of 2 (W - 1).
+// Either way every rank computes bit-identical outputs and no thread waits on
+// more than the rows it is working on.
 //
 // Slot reuse: a region of slot s written by a remote rank at step e + 2 was
 // last read by its owner at step e.  The writer reaches step e + 2 only after
-// its step e + 1 kernel finished, which waited for a step e + 1 flag that the
-// reader raises only in its step e + 1 kernel (in owner mode the final rows
-// wait for the partials' flags of the same step and vice versa), and that
-// kernel starts after the reader's step e kernel completed.  So two slots
-// need no second handshake.  Waits are bounded (2 s per launch): on expiry
-// the status word gets 8 and the rows affected are NaN.
+// its step e + 1 kernel finished, and that kernel waited for words the reader
+// wrote in its own step e + 1 kernel (push: the reader's partial; owner mode:
+// the final rows, or the partial that the final rows' owner waited for),
+// which starts after the reader's step e kernel completed.  So two slots need
+// no second handshake.  Waits are bounded (2 s per launch): on expiry the
+// status word gets 8 and the rows affected are NaN.
 #include "attn_epilogue.cuh"
 #include "attn_kernels.cuh"
 #include "common.cuh"
@@ -47,14 +51,6 @@
 namespace tv {
 namespace {
 
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -62,17 +58,22 @@ __device__ __forceinline__ unsigned long long now_ns() {
 }
 
 constexpr int kThreads = 128;
+// Blocks per SM of the exchange kernel (its registers allow) -- the grid is
+// capped so that all blocks are resident at once: a thread waits for words
+// that the peers' blocks of the same index write.
+constexpr int blocks_per_sm(int world) { return world > 4 ? 3 : 4; }
+constexpr int kMaxGrid = 4 * kNumSMs;
+
+using u64 = unsigned long long;
 
 // Byte offsets inside one rank's exchange buffer.
 struct ExLayout {
   int64_t rows;          // query rows of one partial
-  int64_t lse_off;       // partials' LSE array inside a slot
-  int64_t fin_off;       // final O inside a slot
-  int64_t fin_lse_off;   // final LSE inside a slot
+  int64_t lse_off;       // partials' LSE words inside a slot
+  int64_t fin_off;       // final O words inside a slot
+  int64_t fin_lse_off;   // final LSE words inside a slot
   int64_t slot_bytes;
-  int64_t flags_off;     // int32 [2][W][nrb]
-  int64_t fin_flags_off; // int32 [2][nrb]
-  int64_t words_off;     // int32 [steps completed, blocks finished]
+  int64_t steps_off;     // int32 step count per block
   int64_t total;
   int nrb;               // row blocks
 };
@@ -84,15 +85,56 @@ ExLayout layout(int world, int64_t rows, int D) {
   const int rpb = kThreads / (D / 4);
   L.rows = rows;
   L.nrb = (int)((rows + rpb - 1) / rpb);
-  L.lse_off = align256((int64_t)world * rows * D * 4);
-  L.fin_off = L.lse_off + align256((int64_t)world * rows * 4);
-  L.fin_lse_off = L.fin_off + align256(rows * D * 4);
-  L.slot_bytes = L.fin_lse_off + align256(rows * 4);
-  L.flags_off = 2 * L.slot_bytes;
-  L.fin_flags_off = L.flags_off + align256((int64_t)2 * world * L.nrb * 4);
-  L.words_off = L.fin_flags_off + align256((int64_t)2 * L.nrb * 4);
-  L.total = L.words_off + 256;
+  L.lse_off = align256((int64_t)world * rows * D * 8);
+  L.fin_off = L.lse_off + align256((int64_t)world * rows * 8);
+  L.fin_lse_off = L.fin_off + align256(rows * D * 8);
+  L.slot_bytes = L.fin_lse_off + align256(rows * 8);
+  L.steps_off = 2 * L.slot_bytes;
+  L.total = L.steps_off + align256(4 * kMaxGrid);
   return L;
+}
+
+__device__ __forceinline__ u64 ll_word(float v, int e) {
+  return ((u64)(unsigned)e << 32) | __float_as_uint(v);
+}
+// Four values of step e at dst (32-byte aligned), as two 16-byte stores of
+// two single-copy-atomic words each.
+__device__ __forceinline__ void ll_put4(u64* dst, float4 v, int e) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(ll_word(v.x, e)), "l"(ll_word(v.y, e))
+               : "memory");
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(ll_word(v.z, e)), "l"(ll_word(v.w, e))
+               : "memory");
+}
+__device__ __forceinline__ void ll_put1(u64* dst, float v, int e) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(ll_word(v, e)) : "memory");
+}
+// Bounded waits until the words carry step >= e; false once the launch's
+// deadline has passed.
+__device__ __forceinline__ bool ll_get4(const u64* src, int e, unsigned long long deadline, float4& v) {
+  unsigned it = 0;
+  for (;;) {
+    u64 a, b, c, d;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(src) : "memory");
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(c), "=l"(d) : "l"(src + 2) : "memory");
+    if ((int)(a >> 32) >= e && (int)(b >> 32) >= e && (int)(c >> 32) >= e && (int)(d >> 32) >= e) {
+      v = make_float4(__uint_as_float((unsigned)a), __uint_as_float((unsigned)b), __uint_as_float((unsigned)c),
+                      __uint_as_float((unsigned)d));
+      return true;
+    }
+    if ((++it & 63u) == 0 && now_ns() > deadline) return false;
+  }
+}
+__device__ __forceinline__ bool ll_get1(const u64* src, int e, unsigned long long deadline, float& v) {
+  unsigned it = 0;
+  for (;;) {
+    u64 a;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(src) : "memory");
+    if ((int)(a >> 32) >= e) {
+      v = __uint_as_float((unsigned)a);
+      return true;
+    }
+    if ((++it & 63u) == 0 && now_ns() > deadline) return false;
+  }
 }
 
 struct PeerBases {
@@ -123,148 +165,99 @@ __device__ __forceinline__ void merge_ranks(const float (&l)[W], const float4 (&
   o = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
 }
 
-// Bounded wait until *flag >= e; false once the launch's deadline passed.
-__device__ __forceinline__ bool wait_flag(const int* flag, int e, unsigned long long deadline) {
-  unsigned it = 0;
-  while (ld_acquire_sys(flag) < e) {
-    if ((++it & 255u) == 0 && now_ns() > deadline) return false;
-  }
-  return true;
-}
-
 template <typename T, int D, int W, bool OWNED>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads, blocks_per_sm(W))
     sharded_combine_kernel(const AttnParams p, const PeerBases pb, int rank, const ExLayout L) {
   constexpr int TPR = D / 4;            // threads per row, one float4 of O each
   constexpr int RPB = kThreads / TPR;   // rows per row block
   char* const mine = pb.base[rank];
-  int* const words = reinterpret_cast<int*>(mine + L.words_off);
-  // Every block reads the step count before any block can advance it (the
-  // last block to finish does, below).
-  const int e = *reinterpret_cast<volatile int*>(words) + 1;
-  const int slot = e & 1;
-  const int64_t slot_off = slot * L.slot_bytes;
+  // Every launch over this buffer has the same grid and advances each block's
+  // own count once, so all blocks agree on the step.
+  int* const steps = reinterpret_cast<int*>(mine + L.steps_off);
+  const int e = *reinterpret_cast<volatile int*>(steps + blockIdx.x) + 1;
+  const int64_t slot_off = (e & 1) * L.slot_bytes;
   const unsigned long long deadline = now_ns() + 2000000000ull;
   const int q = threadIdx.x % TPR;
-  const int t = threadIdx.x;
   const float nan = __int_as_float(0x7fc00000);
-  // flags[slot][src][rb] and fin_flags[slot][rb] of the buffer at `base`
-  auto part_flag = [&](char* base, int src, int rb) {
-    return reinterpret_cast<int*>(base + L.flags_off) + ((int64_t)slot * W + src) * L.nrb + rb;
+  auto part_o = [&](char* base, int src, int64_t row) {
+    return reinterpret_cast<u64*>(base + slot_off) + ((int64_t)src * L.rows + row) * D + 4 * q;
   };
-  auto fin_flag = [&](char* base, int rb) {
-    return reinterpret_cast<int*>(base + L.fin_flags_off) + (int64_t)slot * L.nrb + rb;
+  auto part_l = [&](char* base, int src, int64_t row) {
+    return reinterpret_cast<u64*>(base + slot_off + L.lse_off) + (int64_t)src * L.rows + row;
   };
+  auto fin_o = [&](char* base, int64_t row) {
+    return reinterpret_cast<u64*>(base + slot_off + L.fin_off) + row * D + 4 * q;
+  };
+  auto fin_l = [&](char* base, int64_t row) {
+    return reinterpret_cast<u64*>(base + slot_off + L.fin_lse_off) + row;
+  };
+  bool all_ok = true;
   for (int rb = blockIdx.x; rb < L.nrb; rb += gridDim.x) {
     const int64_t row = (int64_t)rb * RPB + threadIdx.x / TPR;
-    const bool valid = row < L.rows;
+    if (row >= L.rows) continue;
     const int owner = OWNED ? (int)((int64_t)rb * W / L.nrb) : rank;
-    int bh = 0, r = 0;
-    float4 own = make_float4(0.f, 0.f, 0.f, 0.f);
-    float own_l = -INFINITY;
-    if (valid) {
-      bh = (int)(row / p.R);
-      r = (int)(row - (int64_t)bh * p.R);
-      combine_split_row<D>(p, bh, r, q, own, own_l);
+    const int bh = (int)(row / p.R);
+    const int r = (int)(row - (int64_t)bh * p.R);
+    float4 own;
+    float own_l;
+    combine_split_row<D>(p, bh, r, q, own, own_l);
+#pragma unroll
+    for (int pr = 0; pr < W; ++pr) {
+      if (pr == rank || (OWNED && pr != owner)) continue;
+      ll_put4(part_o(pb.base[pr], rank, row), own, e);
+      if (q == 0) ll_put1(part_l(pb.base[pr], rank, row), own_l, e);
+    }
+    bool ok = true;
+    float4 o;
+    float lse;
+    if (owner == rank) {
+      float l[W];
+      float4 v[W];
 #pragma unroll
       for (int pr = 0; pr < W; ++pr) {
-        if (pr == rank || (OWNED && pr != owner)) continue;
-        char* dst = pb.base[pr] + slot_off;
-        reinterpret_cast<float4*>(dst)[((int64_t)rank * L.rows + row) * TPR + q] = own;
-        if (q == 0) reinterpret_cast<float*>(dst + L.lse_off)[(int64_t)rank * L.rows + row] = own_l;
+        if (pr == rank) {
+          l[pr] = own_l;
+          v[pr] = own;
+        } else {
+          ok = ll_get4(part_o(mine, pr, row), e, deadline, v[pr]) && ok;
+          ok = ll_get1(part_l(mine, pr, row), e, deadline, l[pr]) && ok;
+        }
       }
-    }
-    __syncthreads();   // the block's pushes precede each flag's release
-    int ok = 1;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    float lse = -INFINITY;
-    if (owner == rank) {
-      if (t < W && t != rank) {
-        if (!OWNED) {
-          __threadfence_system();
-          st_release_sys(part_flag(pb.base[t], rank, rb), e);
-        }
-        ok = wait_flag(part_flag(mine, t, rb), e, deadline);
-      }
-      ok = __syncthreads_and(ok);
-      if (valid) {
-        float l[W];
-        float4 v[W];
-        const char* src = mine + slot_off;
-#pragma unroll
-        for (int pr = 0; pr < W; ++pr) {
-          if (pr == rank) {
-            l[pr] = own_l;
-            v[pr] = own;
-          } else {
-            l[pr] = __ldcg(reinterpret_cast<const float*>(src + L.lse_off) + (int64_t)pr * L.rows + row);
-            v[pr] = __ldcg(reinterpret_cast<const float4*>(src) + ((int64_t)pr * L.rows + row) * TPR + q);
-          }
-        }
-        merge_ranks<W>(l, v, o, lse);
-        if (!ok) {
-          o = make_float4(nan, nan, nan, nan);
-          lse = nan;
-        }
+      merge_ranks<W>(l, v, o, lse);
+      if (!ok) {
+        o = make_float4(nan, nan, nan, nan);
+        lse = nan;
       }
       if (OWNED) {
         // Hand the final rows to every other rank.
-        if (valid) {
 #pragma unroll
-          for (int pr = 0; pr < W; ++pr) {
-            if (pr == rank) continue;
-            char* dst = pb.base[pr] + slot_off;
-            reinterpret_cast<float4*>(dst + L.fin_off)[row * TPR + q] = o;
-            if (q == 0) reinterpret_cast<float*>(dst + L.fin_lse_off)[row] = lse;
-          }
-        }
-        __syncthreads();
-        if (t < W && t != rank) {
-          __threadfence_system();
-          st_release_sys(fin_flag(pb.base[t], rb), e);
+        for (int pr = 0; pr < W; ++pr) {
+          if (pr == rank) continue;
+          ll_put4(fin_o(pb.base[pr], row), o, e);
+          if (q == 0) ll_put1(fin_l(pb.base[pr], row), lse, e);
         }
       }
     } else {
-      // Owner mode, a row block of another rank: publish the partial to the
-      // owner, then wait for its final rows.
-      if (t == 0) {
-        __threadfence_system();
-        st_release_sys(part_flag(pb.base[owner], rank, rb), e);
-        ok = wait_flag(fin_flag(mine, rb), e, deadline);
-      }
-      ok = __syncthreads_and(ok);
-      if (valid) {
-        const char* src = mine + slot_off;
-        o = __ldcg(reinterpret_cast<const float4*>(src + L.fin_off) + row * TPR + q);
-        lse = __ldcg(reinterpret_cast<const float*>(src + L.fin_lse_off) + row);
-        if (!ok) {
-          o = make_float4(nan, nan, nan, nan);
-          lse = nan;
-        }
+      // Owner mode, a row block of another rank: its final rows.
+      ok = ll_get4(fin_o(mine, row), e, deadline, o);
+      ok = ll_get1(fin_l(mine, row), e, deadline, lse) && ok;
+      if (!ok) {
+        o = make_float4(nan, nan, nan, nan);
+        lse = nan;
       }
     }
-    if (!ok && t == 0 && p.err) atomicExch(p.err, 8);
-    if (valid) {
-      const int b = bh / p.Hkv;
-      const int hk = bh - b * p.Hkv;
-      int m, h;
-      row_coords(p, hk, r, m, h);
-      store_out_pair<T>(p, b, m, h, 4 * q, o.x, o.y);
-      store_out_pair<T>(p, b, m, h, 4 * q + 2, o.z, o.w);
-      if (q == 0) store_row_stats<T>(p, b, m, h, lse);
-    }
+    all_ok = all_ok && ok;
+    const int b = bh / p.Hkv;
+    const int hk = bh - b * p.Hkv;
+    int m, h;
+    row_coords(p, hk, r, m, h);
+    store_out_pair<T>(p, b, m, h, 4 * q, o.x, o.y);
+    store_out_pair<T>(p, b, m, h, 4 * q + 2, o.z, o.w);
+    if (q == 0) store_row_stats<T>(p, b, m, h, lse);
   }
-  // The last block to finish advances the step count and resets the
-  // finished-blocks word for the next step.
-  __syncthreads();
-  if (t == 0) {
-    __threadfence();
-    if (atomicAdd(words + 1, 1) == (int)gridDim.x - 1) {
-      words[1] = 0;
-      words[0] = e;
-      __threadfence();
-    }
-  }
+  if (!all_ok && p.err) atomicExch(p.err, 8);
+  __syncthreads();   // every thread has read this block's step count
+  if (threadIdx.x == 0) steps[blockIdx.x] = e;
 }
 
 template <typename T, int D, bool OWNED>
@@ -297,10 +290,11 @@ int launch_sharded_combine(const AttnParams& p, int dtype, int D, int world, int
   const ExLayout L = layout(world, (int64_t)p.B * p.Hkv * p.R, D);
   PeerBases pb;
   for (int r = 0; r < kMaxPeers; ++r) pb.base[r] = r < world ? static_cast<char*>(const_cast<void*>(bases[r])) : nullptr;
-  // Every block of the grid must be resident at once (a block waits for the
-  // peers' blocks of the same row blocks): at most 4 blocks of 128 threads
-  // per SM, each looping over row blocks.
-  const int grid = L.nrb < 4 * kNumSMs ? L.nrb : 4 * kNumSMs;
+  // Every block of the grid must be resident at once: at most
+  // blocks_per_sm(world) blocks of 128 threads per SM, each looping over row
+  // blocks.
+  const int cap = blocks_per_sm(world) * kNumSMs;
+  const int grid = L.nrb < cap ? L.nrb : cap;
   owned = owned && world > 1;
   if (dtype == TV_BF16) {
     if (owned) launch_t<__nv_bfloat16, true>(D, world, dim3(grid), p, pb, rank, L, st);

@@ -142,8 +142,8 @@ class SequenceShardedVerify:
         ``peer_mode`` (peer exchange): ``"push"`` (every rank's partial to
         every peer, one hop), ``"owner"`` (each row block's partials to the
         rank owning it, which hands the final rows back: two hops, less
-        NVLink traffic from three ranks on) or ``"auto"`` (= push, the faster
-        one measured at two ranks)."""
+        NVLink traffic from four ranks on) or ``"auto"`` (push below four
+        ranks, owner from four on)."""
         if peer_mode not in self._PEER_MODES:
             raise ValueError(f"peer_mode must be one of {sorted(self._PEER_MODES)}")
         self.peer_bits = self._PEER_MODES[peer_mode]

@@ -152,7 +152,7 @@ def test_sharded_entry_one_rank_equals_verify_attn(prefix_len, num_splits):
 @pytest.mark.parametrize("mode", [32, 64])                  # owner exchange, push to all
 def test_sharded_entry_gives_up_on_a_silent_peer(mode):
     """Two ranks, but the 'peer' buffer is local memory that no rank ever
-    flags: every wait runs out (2 s), the status word reads 8 and the
+    writes: every wait runs out (2 s), the status word reads 8 and the
     outputs are NaN instead of a silent one-rank result.  In owner mode
     rank 0 owns half the row blocks (waits for the peer's partials) and
     waits for the peer's final rows on the other half."""
@@ -164,3 +164,53 @@ def test_sharded_entry_gives_up_on_a_silent_peer(mode):
     out, lse = _sharded_call(w, bits, [mine.data_ptr(), silent.data_ptr()], 2, 0, status=status, kernel=mode)
     assert int(status.item()) == 8
     assert torch.isnan(out.float()).all() and torch.isnan(lse).all()
+
+
+def _slot_layout(world, rows, d):
+    """Byte offsets of one exchange-buffer slot: [world][rows][d] partial O
+    words, [world][rows] partial LSE words, then the final rows (8-byte words:
+    fp32 bits low, step number high)."""
+    a = lambda x: (x + 255) & ~255
+    lse = a(world * rows * d * 8)
+    fin = lse + a(world * rows * 8)
+    fin_lse = fin + a(rows * d * 8)
+    return {"slot": fin_lse + a(rows * 8), "lse": lse}
+
+
+@pytest.mark.skipif(not cuda_ok(), reason="needs CUDA")
+def test_sharded_entry_exchanges_step_tagged_words():
+    """Push mode, rank 0 of 2 on one GPU.  The 'peer' has already posted its
+    partial for every step (words tagged with a large step number, LSE -inf:
+    nothing to add), so the merge must give the one-rank result bit for bit;
+    and rank 0's own partial must have landed in the peer's buffer as words
+    of step 1 (slot 1) whose LSE halves equal the one-rank LSE."""
+    from specverify.runtime import attention
+    w, bits = _one_gpu_request(1024, seed=7)
+    b, m, h, d = w.q.shape
+    hkv = w.k_pool.shape[1]
+    rows = b * m * h
+    ref = torch.empty_like(w.q)
+    ref_lse = torch.empty(w.q.shape[:3], device="cuda")
+    attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
+              mask_len=m, out=ref, lse=ref_lse)
+    L = _slot_layout(2, rows, d)
+    mine = _exchange_buffer(2, rows, d)
+    peer = _exchange_buffer(2, rows, d)
+    tag = (1 << 30) << 32
+    words = mine.view(torch.int64)
+    for s in (0, 1):
+        o0 = s * L["slot"] // 8
+        words[o0 + rows * d:o0 + 2 * rows * d] = tag                       # rank 1's O: 0.0
+        l0 = (s * L["slot"] + L["lse"]) // 8
+        words[l0 + rows:l0 + 2 * rows] = tag | 0xFF800000                  # rank 1's LSE: -inf
+    out, lse = _sharded_call(w, bits, [mine.data_ptr(), peer.data_ptr()], 2, 0, kernel=64)
+    assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
+    pw = peer.view(torch.int64)
+    o1 = L["slot"] // 8                                                    # slot 1, rank 0's region
+    assert torch.equal(pw[o1:o1 + rows * d] >> 32, torch.ones(rows * d, dtype=torch.int64, device="cuda"))
+    l1 = (L["slot"] + L["lse"]) // 8
+    assert torch.equal(pw[l1:l1 + rows] >> 32, torch.ones(rows, dtype=torch.int64, device="cuda"))
+    lo = peer.view(torch.int32)[2 * l1:2 * (l1 + rows)].view(rows, 2)[:, 0].contiguous().view(torch.float32)
+    # the kernel's row order: (b, kv head, node, group member)
+    want = ref_lse.view(b, m, hkv, h // hkv).permute(0, 2, 1, 3).reshape(-1)
+    assert torch.equal(lo, want)
