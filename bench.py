@@ -12,9 +12,9 @@ heads, head_dim 128), bf16.  Steps rotate over 4 independent layer pools
 
 N = 1 runs config 2 on one GPU.  N > 1 (torchrun, one rank per GPU) runs the
 same 64K problem sequence-sharded: each rank attends its contiguous share of
-the pages; one kernel per rank then pushes its (O, lse) partial into every
-peer's buffer over NVLink and merges all ranks' partials by log-sum-exp, so
-every rank holds the full result ("scaling": "strong": total work fixed).  Time = max over ranks of CUDA-event time.
+the pages; one kernel per rank then exchanges the (O, lse) partials over
+NVLink (to every peer below four ranks, to each row block's owner from four
+on) and merges them by log-sum-exp, so every rank holds the full result ("scaling": "strong": total work fixed).  Time = max over ranks of CUDA-event time.
 
 `value` = algorithmic bytes (every visible K/V row once + Q/O/LSE/page
 table/bitmask) / step time, in GB/s, whole job.  `e2e` measures the same call
@@ -190,7 +190,9 @@ def run_ours(args, rank, world, dev):
                      page_table=shards[i % rotate])
         launches_per_step = 2
         workload = (f"config2 sequence-sharded over {world} GPUs: S=65536 paged, 64-node depth-8 tree, 1 layer, "
-                    f"bf16, partials pushed to every peer over NVLink and merged by one fused kernel per step")
+                    f"bf16, partials exchanged over NVLink as step-tagged words "
+                    f"({'pushed to every peer' if world < 4 else 'merged by each row block owner'}) "
+                    f"and merged by one fused kernel per step")
 
     for _ in range(args.warmup):
         for i in range(rotate):

@@ -183,8 +183,9 @@ int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
  * rank, rows = batch * heads * rows_per_sequence (query rows), allocated so
  * that every rank can address every other rank's buffer (symmetric / IPC
  * memory), 16-byte aligned and zeroed before the first step.  It holds two
- * slots of `world` fp32 partials (O and LSE), per-row-block arrival flags and
- * this rank's step count.
+ * slots of `world` partials (O and LSE, one 8-byte word per value), the
+ * final rows of owner mode and this rank's step counts.  Use one buffer per
+ * (world, rows, head_dim): the layout depends on all three.
  *
  * tv_verify_attn_sharded: `args` is this rank's request exactly as for
  * tv_verify_attn (args->num_keys = this shard's keys) except that out / lse /

@@ -12,11 +12,12 @@ partials are exchanged and every rank merges them in rank order:
 
 Default exchange: NVLink peer memory, one C call per rank
 (``tv_verify_attn_sharded``).  After the attention kernel one kernel combines
-this rank's split partials, stores the result straight into every peer's
-exchange buffer (mapped into every rank through torch symmetric memory),
-raises a flag per row block on each peer, waits on its own buffer for the
-peers' row blocks and merges -- no collective launch, no remote reads, and
-no step-wide barrier.  Fallback (and the host-testable form): ONE NCCL
+this rank's split partials and stores the result straight into the peers'
+exchange buffers (mapped into every rank through torch symmetric memory) as
+8-byte words carrying the value and the step number, waits on its own
+buffer until the peers' words of its rows carry the step, and merges -- no
+collective launch, no remote reads, no flags or fences, and no step-wide
+barrier.  Fallback (and the host-testable form): ONE NCCL
 ``all_gather`` of the packed partials and ``tv_merge_partials``.  Both are
 order-fixed, so every rank gets bit-identical results (the next layer's
 replicated projections need that).  An all-reduce formulation would need a
@@ -88,7 +89,8 @@ def merge_packed(gathered: torch.Tensor, part: PackedPartial, world: int, out_dt
 class PeerExchange:
     """This rank's exchange buffer for ``tv_verify_attn_sharded``, mapped into
     every rank of ``group`` (torch symmetric memory): two slots of all ranks'
-    fp32 partials, per-row-block flags and the step count, zeroed once.
+    partials (8-byte words: value and step number), owner mode's final rows
+    and the per-block step counts, zeroed once.
     Successive steps alternate the slots inside the kernel, so the calls can
     be captured into CUDA graphs and replayed any number of times."""
 
@@ -107,7 +109,7 @@ class PeerExchange:
         self.handle = symm.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
         self.bases = (ctypes.c_void_p * self.world)(*list(self.handle.buffer_ptrs))
         self._ws = None
-        dist.barrier(group)    # every rank's zeroed flags are in place before anyone writes to them
+        dist.barrier(group)    # every rank's buffer is zeroed before any peer writes into it
 
     def run(self, a, device):
         """``tv_verify_attn_sharded`` of the request ``a`` (see ``attn_args``)."""
