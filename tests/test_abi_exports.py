@@ -54,6 +54,27 @@ def test_host_only_calls(lib):
     assert lib.tv_attn_workspace_size(None, None) != 0
 
 
+def test_sharded_exchange_buffer_size(lib):
+    """tv_sharded_exchange_bytes (host arithmetic): two slots, each of W
+    partials' O and LSE plus the final rows as 8-byte words (256-byte aligned
+    sections), then one int32 step count per exchange-kernel block (up to
+    4 x 148), and the argument checks."""
+    f = lib.tv_sharded_exchange_bytes
+    f.restype = ctypes.c_int32
+    f.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64)]
+    a = lambda x: (x + 255) // 256 * 256
+    for world, rows, d in ((1, 2048, 128), (2, 2048, 128), (8, 8192, 64), (3, 7, 32)):
+        n = ctypes.c_int64(-1)
+        assert f(world, rows, d, ctypes.byref(n)) == 0
+        slot = a(world * rows * d * 8) + a(world * rows * 8) + a(rows * d * 8) + a(rows * 8)
+        assert n.value == 2 * slot + a(4 * 4 * 148), (world, rows, d)
+    n = ctypes.c_int64(0)
+    assert f(0, 16, 128, ctypes.byref(n)) != 0           # no ranks
+    assert f(9, 16, 128, ctypes.byref(n)) != 0           # more than 8 ranks
+    assert f(2, 16, 96, ctypes.byref(n)) != 0            # head_dim not 32 / 64 / 128
+    assert f(2, 16, 128, None) != 0
+
+
 def test_ctypes_structs_match_the_header(tmp_path):
     """The ctypes mirrors have the C structs' size and every field offset
     (compiled against include/specverify.h with the host C compiler)."""
