@@ -142,9 +142,12 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 def build_problems(rotate: int, dev, seed: int = 0):
+    return [wl_paged(seed=seed + 100 * i, dev=dev) for i in range(rotate)]
+
+
+def wl_paged(seed: int, dev, root: bool = False):
     from specverify import workloads as wl
-    probs = [wl.paged_verify(seed=seed + 100 * i, device=dev) for i in range(rotate)]
-    return probs
+    return wl.paged_verify(seed=seed, device=dev, root=root)
 
 
 def run_ours(args, rank, world, dev):
@@ -354,6 +357,67 @@ def run_ours(args, rank, world, dev):
                             "copy streams" + ("" if args.no_graph else "; the K steps replayed as one CUDA graph")
                             + ")"}
 
+        if not args.no_graph:
+            # The same pipeline without the graph: every step pays the public
+            # API's host cost (argument packing, checks, tensor-map encoding,
+            # launches) the way an eager serving loop does.
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record()
+            e2e_steps(0, args.steps, held)
+            e1.record()
+            torch.cuda.synchronize()
+            wall = (time.perf_counter() - t0) * 1e3 / args.steps
+            ems_eager = max(e0.elapsed_time(e1) / args.steps, wall)
+            if world > 1:
+                t = torch.tensor([ems_eager], device=dev)
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+                ems_eager = float(t.item())
+            held.clear()
+            e2e["eager"] = {"value": round(alg_bytes / (ems_eager * 1e-3) / 1e9, 1), "unit": "GB/s",
+                            "ms_per_step": round(ems_eager, 4),
+                            "what": "the same pipelined steps issued eagerly (no graph): host cost per call visible"}
+
+    extra = {}
+    if world == 1 and not args.no_extras:
+        from specverify.runtime.tree_attention import describe_attention
+        extra["plan"] = describe_attention(p0.q, p0.k_pool, p0.v_pool, num_keys=p0.num_keys,
+                                           page_table=p0.page_table, mask_bits=bits[0], mask_len=m)
+        # The reference's own verify shape: the root row prepended (M = 65), so
+        # the keys (65536 + 65) end inside a page.
+        rprobs = [wl_paged(seed=100 * i, root=True, dev=dev) for i in range(rotate)]
+        rbits = [pack_tree_mask(p.tree.keep.to(dev)) for p in rprobs]
+        routs = [torch.empty_like(p.q) for p in rprobs]
+
+        def rstep(i):
+            p = rprobs[i]
+            return lambda: attention(p.q, p.k_pool, p.v_pool, num_keys=p.num_keys, page_table=p.page_table,
+                                     mask_bits=rbits[i], mask_len=p.tree.rows, out=routs[i])
+        rms = _timed_graph_steps([rstep(i) for i in range(rotate)], args.steps, args.warmup)
+        ralg = rprobs[0].algorithmic_bytes()
+        extra["with_root_row"] = {
+            "rows": rprobs[0].tree.rows, "num_keys": rprobs[0].num_keys, "ms_per_step": round(rms, 4),
+            "value": round(ralg / (rms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "plan": describe_attention(rprobs[0].q, rprobs[0].k_pool, rprobs[0].v_pool,
+                                       num_keys=rprobs[0].num_keys, page_table=rprobs[0].page_table,
+                                       mask_bits=rbits[0], mask_len=rprobs[0].tree.rows)}
+        del rprobs, rbits, routs
+        torch.cuda.empty_cache()
+        # The reference's GPU sequence for the same step on this GPU.
+        ref_ms, ref_impl, ref_out = reference_gpu_bar(probs, max(3, args.steps // 2), args.warmup)
+        ours_out = verify_attention(p0.q, p0.k_pool, p0.v_pool, p0.prefix_len, p0.tree.keep.to(dev),
+                                    page_table=p0.page_table)
+        extra["reference_gpu"] = {
+            "ms_per_step": round(ref_ms, 4), "value": round(alg_bytes / (ref_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "speedup": round(ref_ms / ms, 2), "prefix": ref_impl, "launch": "eager, as the reference runs it",
+            "max_abs_diff_vs_ours": round(float((ref_out.float() - ours_out.float()).abs().max()), 5),
+            "what": "repeat_kv of the contiguous cache + prefix attention with LSE + masked tree attention with "
+                    "the sigmoid merge weight + in-place merge (llama_target_model.py:793-864) on the same GPU"}
+        torch.cuda.empty_cache()
+
     graphs.clear()   # graphs holding NCCL work are released before the process group goes
     total_bytes = alg_bytes  # whole job: the full 64K problem once per step (sharded or not)
     value = total_bytes / (ms * 1e-3) / 1e9
@@ -398,7 +462,112 @@ def run_ours(args, rank, world, dev):
         "e2e": e2e,
         "clocks": clocks,
     }
+    result.update(extra)
     return result
+
+
+def _timed_graph_steps(step_fns, steps, warmup):
+    """Device ms per step: each step function captured as a CUDA graph,
+    replayed round-robin (the inputs rotate), CUDA events on the stream."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for f in step_fns:
+            f()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graphs = []
+    for f in step_fns:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            f()
+        graphs.append(g)
+    for i in range(max(warmup, len(graphs))):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        graphs[i % len(graphs)].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del graphs
+    return ms
+
+
+def reference_gpu_bar(probs, steps, warmup):
+    """The reference's verify-attention sequence on this GPU, as its own ops
+    (``llama_target_model.py:793-864``): ``repeat_kv`` of the layer's
+    contiguous cache (the reference has no paged kernel, so the pages are
+    gathered once, untimed), prefix attention with LSE through flash-attn's
+    ``flash_attn_with_kvcache`` (``:839-845``; torch's own attention kernels
+    when flash-attn cannot run here), the tree block as masked softmax
+    attention with the ``sigmoid(prefix_lse - tree_lse)`` weight
+    (``tree_attention.py:40-63``, the math of its Triton kernel), and the
+    in-place merge (``:862-864``).  Eager, as the reference runs it."""
+    def repeat_kv(x, n_rep):                               # llama_target_model.py:543-560
+        bb, hh, nn, dd = x.shape
+        return x[:, :, None].expand(bb, hh, n_rep, nn, dd).reshape(bb, hh * n_rep, nn, dd)
+
+    p0 = probs[0]
+    b, m, h, d = p0.q.shape
+    hkv = p0.k_pool.shape[1]
+    g = h // hkv
+    s = p0.prefix_len
+    scale = 1.0 / math.sqrt(d)
+    caches = []
+    for p in probs:
+        k, v = p.contiguous_kv(0)                          # [S+M, Hkv, D]
+        caches.append((k.permute(1, 0, 2)[None].contiguous(), v.permute(1, 0, 2)[None].contiguous(),
+                       p.tree.keep.to(p.q.device).bool()))
+    prefix_impl = None
+    try:
+        from flash_attn import flash_attn_with_kvcache
+        kk = repeat_kv(caches[0][0], g).transpose(1, 2)
+        vv = repeat_kv(caches[0][1], g).transpose(1, 2)
+        o, lse = flash_attn_with_kvcache(p0.q, kk, vv, causal=False, cache_seqlens=s, return_softmax_lse=True)
+        torch.cuda.synchronize()
+        prefix_impl = "flash_attn.flash_attn_with_kvcache"
+    except Exception as exc:                               # flash-attn not built for this GPU
+        log(f"reference_gpu: flash-attn unavailable here ({type(exc).__name__}: {exc}); torch attention instead")
+
+    def step(i):
+        p = probs[i % len(probs)]
+        kc, vc, keep = caches[i % len(caches)]
+        kk = repeat_kv(kc, g)                              # [B, H, S+M, D], written and re-read
+        vv = repeat_kv(vc, g)
+        q_flash = p.q
+        if prefix_impl:
+            p_out, p_lse = flash_attn_with_kvcache(q_flash, kk.transpose(1, 2), vv.transpose(1, 2), causal=False,
+                                                   cache_seqlens=s, return_softmax_lse=True)
+        else:
+            p_out, p_lse, *_ = torch.ops.aten._scaled_dot_product_efficient_attention(
+                q_flash.transpose(1, 2), kk[:, :, :s], vv[:, :, :s], None, True, scale=scale)
+            p_out = p_out.transpose(1, 2)
+        qt = q_flash.transpose(1, 2).float()               # [B, H, M, D]
+        sc = torch.matmul(qt, kk[:, :, s:].float().transpose(-2, -1)) * scale
+        sc = sc.masked_fill(~keep[None, None], float("-inf"))
+        t_lse = torch.logsumexp(sc, dim=-1)                # [B, H, M]
+        t_out = torch.matmul(torch.softmax(sc, dim=-1).to(q_flash.dtype), vv[:, :, s:]).transpose(1, 2)
+        w = torch.sigmoid(p_lse - t_lse).transpose(1, 2)[..., None].to(q_flash.dtype)
+        out = t_out.contiguous()
+        out.mul_(1.0 - w)
+        out.add_(p_out.to(out.dtype).mul_(w))
+        return out
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    out = step(0)
+    return ms, prefix_impl or "torch efficient attention (aten._scaled_dot_product_efficient_attention)", out
 
 
 # ---------------------------------------------------------------------------
@@ -804,6 +973,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the side measurements (root-row variant, reference GPU ops)")
     ap.add_argument("--workload", choices=["verify", "rope-append", "lmhead-accept", "tree-finalize",
                                            "chunk-retrieve"], default="verify")
     args = ap.parse_args()

@@ -134,14 +134,21 @@ typedef struct tv_attn_args {
   void* weight;                  /* required when aux_lse != NULL           */
   int64_t w_sb, w_sm, w_sh;
   int32_t num_splits;            /* 0 = choose automatically                */
-  int32_t kernel;                /* bits 0-3: 0 auto, 1 warp-MMA, 2 tcgen05;
+  int32_t kernel;                /* bits 0-3: 0 auto, 1 warp-MMA, 2 tcgen05
+                                    only (TV_ERR_UNSUPPORTED when the request
+                                    does not fit it);
                                     bit 4 (16): softmax weights as a hi+lo
                                     16-bit pair in the PV product (automatic
                                     for num_keys <= 4096);
                                     tv_verify_attn_sharded only: bit 5 (32)
                                     owner exchange, bit 6 (64) push to every
                                     peer (default: push below 4 ranks,
-                                    owner from 4 on)                       */
+                                    owner from 4 on);
+                                    bit 7 (128): tcgen05 path on a paged
+                                    pool loads each 64-dim half of a page
+                                    row as its own TMA box (default: one box
+                                    for both halves when the pool's page and
+                                    head strides allow it)                 */
   void* workspace;
   size_t workspace_bytes;
   int32_t* status;               /* optional device word, zeroed by the caller;
@@ -151,6 +158,14 @@ typedef struct tv_attn_args {
 
 int tv_attn_workspace_size(const tv_attn_args* args, size_t* bytes);
 int tv_verify_attn(const tv_attn_args* args, void* stream);
+
+/* The plan tv_verify_attn would run for `args` (host only, nothing launched):
+ * info[0] = kernel (1 warp-MMA, 2 tcgen05), info[1] = key splits,
+ * info[2] = 1 when the tcgen05 kernel loads whole-head (both 64-dim halves)
+ * TMA boxes, info[3] = 1 when the warp-MMA kernel runs split-P.  No
+ * counterpart in the reference (its kernel choice is fixed per call site,
+ * llama_target_model.py:836-845). */
+int tv_attn_describe(const tv_attn_args* args, int32_t* info);
 
 /* tv_verify_attn without a caller workspace: no counterpart in the reference
  * (its attention allocates its temporaries per call).  The split partials
@@ -204,13 +219,18 @@ int tv_merge_partials(int32_t parts, int64_t rows, int32_t head_dim,
  * 2 (W-1), for a second hop).  Merges run by log-sum-exp in rank order:
  * every rank gets bit-identical outputs.  args->kernel bits 5 / 6 pick the
  * mode (default: push below 4 ranks, owner from 4 on).
- * bases[r] = rank r's exchange buffer as mapped in this process (world <= 8).
- * Every rank must make the same sequence of calls with the same shapes;
- * successive calls alternate the buffer's two slots by themselves. */
+ * A word is accepted only when it carries this call's step: a later step
+ * means a peer gave up on this rank and moved on, and the rows are flagged
+ * (status 8, NaN) rather than merged.
+ * bases[r] = rank r's exchange buffer as mapped in this process (world <= 8);
+ * exchange_bytes = the size of each (exactly tv_sharded_exchange_bytes for
+ * this request's world, rows and head_dim, else TV_ERR_WORKSPACE before any
+ * launch).  Every rank must make the same sequence of calls with the same
+ * shapes; successive calls alternate the buffer's two slots by themselves. */
 int tv_sharded_exchange_bytes(int32_t world, int64_t rows, int32_t head_dim, int64_t* bytes);
 int tv_verify_attn_sharded_workspace_size(const tv_attn_args* args, size_t* bytes);
 int tv_verify_attn_sharded(const tv_attn_args* args, int32_t world, int32_t rank, const void* const* bases,
-                           void* stream);
+                           int64_t exchange_bytes, void* stream);
 
 /* ---- masks --------------------------------------------------------------
  * Pack a [batch][rows][cols] keep-mask into bits: bit c of row r is set when

@@ -13,9 +13,6 @@
 namespace tv {
 
 static thread_local std::string g_last_cuda_error;
-static long long* g_trace = nullptr;   // profiling aid: per-tile timestamps of CTA 0
-
-extern "C" void tv_debug_set_trace(long long* device_buffer) { g_trace = device_buffer; }
 
 int record_cuda_error(cudaError_t e) {
   g_last_cuda_error = cudaGetErrorString(e);
@@ -156,12 +153,10 @@ Plan plan(const tv_attn_args* a) {
   if (paged) while ((1 << shift) < a->page_size) ++shift;
   Plan pl;
   const int sel = a->kernel & 15;
-  // The tensor-memory kernel takes long, uniform-length key ranges whose last
-  // TMA box ends on a page / tile boundary (keys past the end are then whole
-  // out-of-range boxes, which TMA fills with zeros).
-  const int box = paged ? (a->page_size < tc_tile_keys() ? a->page_size : tc_tile_keys()) : 1;
+  // The tensor-memory kernel takes long, uniform-length key ranges (any
+  // length: it zeroes the unused rows of a last page that ends mid-tile).
   pl.tc = (sel != 1) && !(a->kernel & 16) && !a->kv_lens && a->num_keys > kPreciseMaxKeys &&
-          (a->num_keys % box) == 0 && tc_supported(a->dtype, D, R, paged, shift);
+          tc_supported(a->dtype, D, R, paged, shift);
   pl.tile = pl.tc ? tc_tile_keys() : mma_tile_keys();
   const int row_blocks = pl.tc ? tc_row_blocks(R) : (R + mma_rows_per_cta() - 1) / mma_rows_per_cta();
   const int64_t base = (int64_t)row_blocks * a->batch * a->kv_heads;
@@ -179,6 +174,9 @@ Plan plan(const tv_attn_args* a) {
   pl.splits = tiles > 0 ? (tiles + pl.tiles_per_split - 1) / pl.tiles_per_split : 1;
   return pl;
 }
+
+// kernel selector 2 asks for the tensor-memory kernel and nothing else.
+bool plan_allowed(const tv_attn_args* a, const Plan& pl) { return (a->kernel & 15) != 2 || pl.tc; }
 
 // Bytes of `splits` partials: O [splits][rows][D] fp32 (256-byte aligned end),
 // then LSE [splits][rows] fp32.
@@ -230,7 +228,6 @@ void fill_params(const tv_attn_args* a, const Plan& pl, bool partials, AttnParam
   p.weight = a->weight;
   p.w_sb = a->w_sb; p.w_sm = a->w_sm; p.w_sh = a->w_sh;
   p.err = a->status;
-  p.trace = g_trace;
   if (partials) {
     const int64_t rows = (int64_t)p.B * p.Hkv * p.R;
     const size_t o = (size_t)pl.splits * rows * a->head_dim * sizeof(float);
@@ -243,7 +240,7 @@ void fill_params(const tv_attn_args* a, const Plan& pl, bool partials, AttnParam
 // average the bf16 rounding of P away.  Bit 4 of `kernel` forces it.
 int launch_attention(const tv_attn_args* a, const Plan& pl, const AttnParams& p, cudaStream_t st) {
   const bool precise = (a->kernel & 16) || a->num_keys <= kPreciseMaxKeys;
-  return pl.tc ? launch_attn_tc(p, a->dtype, a->head_dim, st)
+  return pl.tc ? launch_attn_tc(p, a->dtype, a->head_dim, a->kernel, st)
                : launch_attn_mma(p, a->dtype, a->head_dim, precise, st);
 }
 
@@ -296,7 +293,9 @@ int tv_attn_workspace_size(const tv_attn_args* a, size_t* bytes) {
   const int v = validate(a);
   if (v != TV_OK) return v;
   if (a->batch == 0 || a->rows == 0) return TV_OK;
-  *bytes = workspace_for(a, plan(a));
+  const Plan pl = plan(a);
+  if (!plan_allowed(a, pl)) return TV_ERR_UNSUPPORTED;
+  *bytes = workspace_for(a, pl);
   return TV_OK;
 }
 
@@ -305,6 +304,7 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
   if (v != TV_OK) return v;
   if (a->batch == 0 || a->rows == 0) return TV_OK;
   const Plan pl = plan(a);
+  if (!plan_allowed(a, pl)) return TV_ERR_UNSUPPORTED;
   const size_t need = workspace_for(a, pl);
   if (need > 0 && (!a->workspace || a->workspace_bytes < need)) return TV_ERR_WORKSPACE;
   if (need > 0 && !aligned16(a->workspace)) return TV_ERR_ALIGN;
@@ -317,18 +317,37 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
   return rc;
 }
 
+int tv_attn_describe(const tv_attn_args* a, int32_t* info) {
+  if (!info) return TV_ERR_NULL;
+  info[0] = info[1] = info[2] = info[3] = 0;
+  const int v = validate(a);
+  if (v != TV_OK) return v;
+  if (a->batch == 0 || a->rows == 0) return TV_OK;
+  const Plan pl = plan(a);
+  if (!plan_allowed(a, pl)) return TV_ERR_UNSUPPORTED;
+  AttnParams p;
+  fill_params(a, pl, pl.splits > 1, p);
+  info[0] = pl.tc ? 2 : 1;
+  info[1] = pl.splits;
+  info[2] = pl.tc && a->page_table ? attn_tc_wide(p, a->dtype, a->kernel) : 0;
+  info[3] = pl.tc ? 0 : ((a->kernel & 16) || a->num_keys <= kPreciseMaxKeys ? 1 : 0);
+  return TV_OK;
+}
+
 int tv_verify_attn_sharded_workspace_size(const tv_attn_args* a, size_t* bytes) {
   if (!bytes) return TV_ERR_NULL;
   *bytes = 0;
   const int v = validate(a);
   if (v != TV_OK) return v;
   if (a->batch == 0 || a->rows == 0) return TV_OK;
-  *bytes = partial_bytes(a, plan(a).splits);
+  const Plan pl = plan(a);
+  if (!plan_allowed(a, pl)) return TV_ERR_UNSUPPORTED;
+  *bytes = partial_bytes(a, pl.splits);
   return TV_OK;
 }
 
 int tv_verify_attn_sharded(const tv_attn_args* a, int32_t world, int32_t rank, const void* const* bases,
-                           void* stream) {
+                           int64_t exchange_bytes, void* stream) {
   const int v = validate(a);
   if (v != TV_OK) return v;
   if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world) return TV_ERR_SHAPE;
@@ -338,7 +357,13 @@ int tv_verify_attn_sharded(const tv_attn_args* a, int32_t world, int32_t rank, c
     if (!aligned16(bases[r])) return TV_ERR_ALIGN;
   }
   if (a->batch == 0 || a->rows == 0) return TV_OK;
+  // The buffers' layout (slots, step counts per block of the exchange grid)
+  // follows from (world, rows, head_dim): a buffer made for another shape
+  // would take stores past its end or desynchronise the step counts.
+  if (exchange_bytes != sharded_exchange_bytes(world, (int64_t)a->batch * a->rows * a->heads, a->head_dim))
+    return TV_ERR_WORKSPACE;
   const Plan pl = plan(a);
+  if (!plan_allowed(a, pl)) return TV_ERR_UNSUPPORTED;
   const size_t need = partial_bytes(a, pl.splits);
   if (!a->workspace || a->workspace_bytes < need) return TV_ERR_WORKSPACE;
   if (!aligned16(a->workspace)) return TV_ERR_ALIGN;

@@ -14,11 +14,14 @@ int mma_tile_keys();
 int mma_rows_per_cta();
 
 // Tensor-memory (tcgen05) path: head_dim 128, >= 64 query rows per KV head.
-int launch_attn_tc(const AttnParams& p, int dtype, int D, cudaStream_t st);
+// kernel_bits: tv_attn_args.kernel (bit 7 forces half-head TMA boxes).
+int launch_attn_tc(const AttnParams& p, int dtype, int D, int kernel_bits, cudaStream_t st);
+// 1 when launch_attn_tc would load whole-head (wide) TMA boxes for p.
+int attn_tc_wide(const AttnParams& p, int dtype, int kernel_bits);
 bool tc_supported(int dtype, int D, int R, bool paged, int page_shift);
 int tc_tile_keys();
 int tc_rows_per_cta();
-int tc_row_blocks(int R);   // CTAs per (batch, KV head); pairs above 128 rows
+int tc_row_blocks(int R);   // CTAs per (batch, KV head)
 
 // Log-sum-exp merge of split partials into the final outputs of AttnParams.
 int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st);
@@ -31,5 +34,7 @@ int launch_split_combine(const AttnParams& p, int dtype, int D, cudaStream_t st)
 constexpr int kMaxPeers = 8;
 int launch_sharded_combine(const AttnParams& p, int dtype, int D, int world, int rank, const void* const* bases,
                            bool owned, cudaStream_t st);
+// Bytes of one rank's exchange buffer (the layout launch_sharded_combine uses).
+int64_t sharded_exchange_bytes(int world, int64_t rows, int D);
 
 }  // namespace tv

@@ -41,7 +41,6 @@ struct AttnParams {
   float* part_o;
   float* part_lse;
   int* err;                // optional device status word (nonzero = a wait gave up)
-  long long* trace;        // optional per-tile timestamps of one CTA (profiling aid)
 };
 
 }  // namespace tv

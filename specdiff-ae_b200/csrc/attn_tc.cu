@@ -3,24 +3,27 @@
 //
 // A CTA holds 128 query rows of one (batch, KV head) -- tree nodes times the
 // query heads of the GQA group -- and streams one split of the keys in
-// 128-key tiles.  Groups of more than 128 rows run as CTA pairs (a cluster
-// of two, tcgen05 cta_group::2, M = 256): each CTA loads only its half of
-// every K tile (64 keys) and of every V tile (64 head-dim columns), and one
-// MMA spans both CTAs' rows, so each K/V byte crosses from L2 to an SM once
-// and the TMA work per SM halves.  A single CTA (cta_group::1) loads whole
-// tiles.
+// 128-key tiles.  The row blocks of one KV head (two at 64 nodes x GQA 4) are
+// launched as one cluster so they run on one GPC and share the K/V tiles in
+// L2.
 //
 //   warps 0, 10  TMA producers, all 32 lanes: warp 0 loads K, warp 10 loads V,
-//             each with its own ring cursor.  A box is one chunk of 16 tokens
-//             (a page) times one 64-wide half of head_dim, read straight from
-//             the paged pool through the page table (page ids a tile ahead)
-//             into 128-byte-swizzled tiles; the boxes of a tile are spread
-//             over the lanes.  Missing pages are fetched at an out-of-range
-//             page index, which TMA fills with zeros.
-//   warps 11, 1  MMA issuers (one thread each, in the pair's first CTA):
-//             S = Q K^T (A = Q, B = K from shared memory, fp32 accumulator in
-//             TMEM) and O += P V (A = P read from TMEM, B = V from shared
-//             memory), each issued as soon as its inputs are ready.
+//             each with its own ring cursor.  A box is one chunk of up to 16
+//             tokens read straight from the paged pool through the page table
+//             (page ids a tile ahead) into 128-byte-swizzled tiles; the boxes
+//             of a tile are spread over the lanes.  "Wide" boxes carry both
+//             64-dim halves of a chunk (4 KB at 16 tokens), "narrow" ones one
+//             half (2 KB); wide needs a pool whose page index and head index
+//             merge into one stride (the reference's [P, Hkv, page, D]).
+//             Missing pages are fetched at an out-of-range index, which TMA
+//             fills with zeros.
+//   warps 11, 1  MMA issuers (one thread each): S = Q K^T (A = Q, B = K from
+//             shared memory, fp32 accumulator in TMEM) and O += P V (A = P
+//             read from TMEM, B = V from shared memory), each issued as soon
+//             as its inputs are ready.  Before the PV of a tile that ends
+//             inside a page, the PV issuer zeroes the V rows past the last
+//             key (the page's unused slots may hold anything, and 0 * NaN is
+//             NaN).
 //   warps 2-9 softmax: warps 2-5 take the even tiles, warps 6-9 the odd ones;
 //             warp w covers TMEM lane quarter w % 4, and each thread owns one
 //             query row and all 128 keys of its tiles.  The running reference
@@ -35,8 +38,8 @@
 // it just finished.
 //
 // Every mbarrier wait is bounded (2 s); on expiry the CTA raises an abort
-// flag (in both CTAs of a pair), records a status word, poisons its rows with
-// NaN, unwinds and frees its tensor memory.
+// flag, records a status word, poisons its rows with NaN, unwinds and frees
+// its tensor memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -56,9 +59,8 @@ constexpr int ROWS = 128;             // query rows per CTA
 constexpr int HD = 128;               // head_dim
 constexpr int SUB = 128 * 128;        // [128 rows][64 dims] swizzled subtile (16 KB)
 constexpr int TILE = 2 * SUB;         // 128 rows x 128 dims (32 KB)
-constexpr int RING = 6 * TILE;        // shared memory of the K and V rings
+constexpr int ST = 3;                 // ring slots of K and of V
 constexpr float kRescale = 8.0f;      // log2 units
-constexpr int MAXST = 6;              // most ring slots
 constexpr int THREADS = 384;          // K producer, PV issuer, 8 softmax warps, V producer, S issuer
 constexpr int SBUF = 2;               // S buffers in TMEM (fp32 scores, 128 columns each)
 constexpr int PBUF = 2;               // P buffers in TMEM (16-bit pairs, 64 columns each)
@@ -66,37 +68,31 @@ constexpr uint32_t TMEM_COLS = 512;   // S0 S1 P0 P1 O
 constexpr uint32_t P_COL = SBUF * BN;
 constexpr uint32_t O_COL = P_COL + PBUF * (BN / 2);
 static_assert(O_COL + 128 == TMEM_COLS, "tensor memory layout");
-constexpr bool kUsePairs = false;   // CTA pairs: the S MMA's cross-SM K reads are slow
 
-// Per-CTA share of the K and V tiles: a pair splits K by keys and V by
-// head-dim columns.
-template <bool PAIR>
-struct Cfg {
-  static constexpr int KROWS = PAIR ? 64 : 128;    // keys of each K tile held here
-  static constexpr int VCOLS = PAIR ? 64 : 128;    // head-dim columns of each V tile held here
-  static constexpr int KSUB = KROWS * 128;         // one 64-dim half of a K slot
-  static constexpr int KSLOT = 2 * KSUB;
-  static constexpr int VSLOT = BN * VCOLS * 2;
-  static constexpr int KST = RING / 2 / KSLOT;     // 3 or 6
-  static constexpr int VST = RING / 2 / VSLOT;
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE;
-  static constexpr int V_OFF = K_OFF + KST * KSLOT;
-  static constexpr int BAR_OFF = V_OFF + VST * VSLOT;
-  static constexpr int SMEM = BAR_OFF + 3072;      // barriers, page ids, row-max exchange
-  static constexpr uint32_t M = PAIR ? 256 : 128;  // MMA rows (both CTAs of a pair)
-  static_assert(KST <= MAXST && VST <= MAXST, "ring depth");
-  static_assert(SMEM <= 227 * 1024, "shared memory budget");
-};
+constexpr int Q_OFF = 0;
+constexpr int K_OFF = TILE;
+constexpr int V_OFF = K_OFF + ST * TILE;
+constexpr int BAR_OFF = V_OFF + ST * TILE;
+constexpr int SMEM = BAR_OFF + 3072;  // barriers, row-max exchange
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+
+// Byte offset of row n (a key), 64-dim half h, inside a K or V slot.
+//   narrow: [half][128 rows][128 B]                (16 KB per half)
+//   wide:   [row / 8][half][row % 8][128 B]        (2 KB per 8-row group)
+// Both are 128-byte-swizzle layouts of 1 KB atoms (8 rows x 128 B).
+template <bool WIDE>
+__host__ __device__ constexpr int row_off(int n, int h) {
+  return WIDE ? (n >> 3) * 2048 + h * 1024 + (n & 7) * 128 : h * SUB + n * 128;
+}
 
 struct Bars {
-  uint64_t k_full[MAXST];   // pair: only the first CTA's are used
-  uint64_t k_empty[MAXST];
-  uint64_t v_full[MAXST];
-  uint64_t v_empty[MAXST];
+  uint64_t k_full[ST];
+  uint64_t k_empty[ST];
+  uint64_t v_full[ST];
+  uint64_t v_empty[ST];
   uint64_t s_full[SBUF];
   uint64_t s_free[SBUF];    // the 4 softmax warps of a tile have read its scores
-  uint64_t p_full[PBUF];    // 4 softmax warps per CTA arrive (pair: on the first CTA's)
+  uint64_t p_full[PBUF];    // 4 softmax warps arrive
   uint64_t pv_done[PBUF];   // per P buffer: PV of the tile in it retired
   uint64_t o_done;
   uint64_t pair[4];         // per TMEM lane quarter: the two softmax warps meet at the end
@@ -109,10 +105,8 @@ struct Bars {
 };
 static_assert(sizeof(Bars) <= 3072, "barrier block");
 
-template <bool PAIR>
 __device__ __forceinline__ void raise_abort(Bars* bars, int* err, int code) {
   bars->abort = 1;
-  if (PAIR) st_cluster_u32(&bars->abort, cluster_rank() ^ 1u, 1u);
   if (err) atomicExch(err, code);
 }
 
@@ -153,28 +147,13 @@ __device__ __forceinline__ void mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint3
       : "memory");
 }
 
-// The same two MMAs issued for a CTA pair (cta_group::2, M = 256): A rows and
-// the B operand's N columns are split between the two CTAs at equal shared
-// memory offsets, D lands in each CTA's tensor memory for its own rows.
-__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
-                                            uint32_t idesc, uint32_t accumulate) {
+// TMA tile load, 5-D map (the wide boxes).
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
-      "mov.b64 ad, {%1, %2};\n\t"
-      "mov.b64 bd, {%3, %4};\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 bd;\n\t"
-      "mov.b64 bd, {%2, %3};\n\t"
-      "setp.ne.b32 p, %5, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], bd, %4, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"((uint32_t)__cvta_generic_to_shared(bar))
       : "memory");
 }
 
@@ -216,14 +195,6 @@ __device__ __forceinline__ float chunk_max(const uint32_t* v) {
   return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
 }
 
-// Every kPolyEvery-th pair of scores takes a polynomial 2^x on the FMA pipe
-// instead of the MUFU ex2 (0 = never): the MUFU unit (16 lanes per clock per
-// SM) is as busy as the tensor pipe on a 128-key tile otherwise.
-#ifndef TV_POLY_EVERY
-#define TV_POLY_EVERY 0
-#endif
-constexpr int kPolyEvery = TV_POLY_EVERY;
-
 // P = exp2(s * sl2 - mu) for 64 scores, packed as 16-bit pairs (key 2k in the
 // low half of word k: the layout the PV MMA reads A from); returns sum of P.
 template <typename T>
@@ -231,77 +202,35 @@ __device__ __forceinline__ float chunk_exp(const uint32_t* v, float sl2, float m
   float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < 64; j += 2) {
-    float p0, p1;
-    if (kPolyEvery > 0 && ((j >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
-      const float2 e = exp2_poly2(make_float2(fmaf(__uint_as_float(v[j]), sl2, -mu), fmaf(__uint_as_float(v[j + 1]), sl2, -mu)));
-      p0 = e.x;
-      p1 = e.y;
-    } else {
-      // scale and shift two scores with one packed f32x2 FMA
-      const float2 x = fma2(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), make_float2(sl2, sl2),
-                            make_float2(-mu, -mu));
-      p0 = fast_exp2(x.x);
-      p1 = fast_exp2(x.y);
-    }
+    // scale and shift two scores with one packed f32x2 FMA
+    const float2 x = fma2(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), make_float2(sl2, sl2),
+                          make_float2(-mu, -mu));
+    const float p0 = fast_exp2(x.x);
+    const float p1 = fast_exp2(x.y);
     s[(j >> 1) & 3] += p0 + p1;
     pk[j >> 1] = pack_pair<T>(p0, p1);
   }
   return (s[0] + s[1]) + (s[2] + s[3]);
 }
 
-template <typename F>
-__device__ __forceinline__ bool timed_wait(long long& acc, F f) {
-  const long long c0 = clock64();
-  const bool r = f();
-  acc += clock64() - c0;
-  return r;
-}
-
-template <typename T, bool PAGED, bool PAIR>
+template <typename T, bool PAGED, bool WIDE>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_tc_kernel(const AttnParams p, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                    int box, int tok_first) {
-  using C = Cfg<PAIR>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte-swizzled TMA tiles need 1 KB alignment; the budget leaves no
-  // room to realign, so an unaligned base is reported instead of used (both
-  // CTAs of a pair see the same layout and leave together).
+  // room to realign, so an unaligned base is reported instead of used.
   if ((smem_u32(smem_raw) & 1023u) != 0) {
     if (threadIdx.x == 0 && p.err) atomicExch(p.err, 7);
     return;
   }
   uint8_t* smem = smem_raw;
-  uint8_t* sQ = smem + C::Q_OFF;
-  uint8_t* sK = smem + C::K_OFF;
-  uint8_t* sV = smem + C::V_OFF;
-  Bars* bars = reinterpret_cast<Bars*>(smem + C::BAR_OFF);
+  uint8_t* sQ = smem + Q_OFF;
+  uint8_t* sK = smem + K_OFF;
+  uint8_t* sV = smem + V_OFF;
+  Bars* bars = reinterpret_cast<Bars*>(smem + BAR_OFF);
   volatile int* abort = &bars->abort;
   int* err = p.err;
-  const uint32_t rank = PAIR ? cluster_rank() : 0u;
-  // Profiling aid, compiled in only with TV_PROFILE_TRACE (and then active
-  // only when the host set a trace buffer): per-CTA start/end times and wait
-  // totals, and per-tile event times of the first CTAs.
-  const int cta_id = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
-#ifdef TV_PROFILE_TRACE
-  long long* cstat = (p.trace && cta_id < 1024) ? p.trace + 1024 + 4096 + cta_id * 16 : nullptr;
-  long long* trace = (p.trace && cta_id < 2) ? p.trace + (cta_id == 0 ? 0 : 1024 + 4096 + 16 * 1024) : nullptr;
-#define TV_TIMED(acc, expr) (cstat ? timed_wait(acc, [&]() { return (expr); }) : (expr))
-#define TV_TRACE(kind, i)                                        \
-  do {                                                           \
-    if (trace && (i) < 64) trace[(kind) * 64 + (i)] = clock64(); \
-  } while (0)
-#else
-  long long* const cstat = nullptr;
-#define TV_TIMED(acc, expr) (expr)
-#define TV_TRACE(kind, i) \
-  do {                    \
-  } while (0)
-#endif
-  (void)cta_id;
-  if (cstat && threadIdx.x == 0) {
-    p.trace[1024 + cta_id * 4] = (long long)global_ns();
-    p.trace[1024 + cta_id * 4 + 2] = clock64();
-  }
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -318,7 +247,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int NT = t1 > t0 ? t1 - t0 : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < MAXST; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
       mbar_init(&bars->v_full[s], 1);
@@ -326,8 +255,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int s = 0; s < SBUF; ++s) {
       mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_free[s], PAIR ? 8 : 4);
-      mbar_init(&bars->p_full[s], PAIR ? 8 : 4);
+      mbar_init(&bars->s_free[s], 4);
+      mbar_init(&bars->p_full[s], 4);
     }
     for (int s = 0; s < PBUF; ++s) mbar_init(&bars->pv_done[s], 1);
     mbar_init(&bars->o_done, 1);
@@ -344,13 +273,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       prefetch_tmap(&tmv);
     }
     __syncwarp();
-    if (PAIR) {
-      tmem_alloc_pair(&bars->tmem, TMEM_COLS);
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(&bars->tmem, TMEM_COLS);
-      tmem_relinquish();
-    }
+    tmem_alloc(&bars->tmem, TMEM_COLS);
+    tmem_relinquish();
   }
 
   // ---- queries -> shared memory, 128-byte swizzled [d-half][row][64] --------
@@ -373,8 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   fence_proxy_async();
   tc_fence_before();
-  if (PAIR) cluster_sync();   // barrier inits of both CTAs visible before any remote arrive
-  else __syncthreads();
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
@@ -384,40 +307,32 @@ __global__ void __launch_bounds__(THREADS, 1)
     // thread keeps about one TMA box in flight (a box costs its issuing
     // thread roughly a memory latency), so a tile's boxes are spread over the
     // lanes, and successive tiles rotate to the next lanes: box j of tile i
-    // goes to lane (i * n + j) mod 32, letting a warp keep two tiles in
-    // flight.  A box is one chunk of `box` tokens (a page, or 16 tokens of a
-    // larger page / contiguous cache) times one 64-wide half of head_dim.
-    // Each warp reads the page ids of the next tile's chunks a tile ahead.
+    // goes to lane (i * n + j) mod 32, letting a warp keep two or more tiles
+    // in flight.  Each warp reads the page ids of the next tile's chunks a
+    // tile ahead.
     if (NT > 0) {
       const bool is_k = warp == 0;
-      const int nst = is_k ? C::KST : C::VST;
-      const int nch_v = BN / box;                      // chunks per tile
-      const int nch = is_k ? C::KROWS / box : nch_v;   // chunks this CTA loads
-      const int ch0 = is_k ? (int)rank * C::KROWS / box : 0;
-      const int nb = is_k ? 2 * nch : (PAIR ? 1 : 2) * nch;   // boxes per tile
+      const int nch = BN / box;                        // chunks per tile
+      const int nb = WIDE ? nch : 2 * nch;             // boxes per tile
       uint64_t* full_ring = is_k ? bars->k_full : bars->v_full;
       uint64_t* empty_ring = is_k ? bars->k_empty : bars->v_empty;
       const CUtensorMap* map = is_k ? &tmk : &tmv;
       uint8_t* base = is_k ? sK : sV;
-      const int slot_bytes = is_k ? C::KSLOT : C::VSLOT;
       // page id of chunk `lane` of tile t (lanes past the tile's chunks: -1)
       auto fetch_page = [&](int t) {
         const int n0 = t * BN + lane * box;
-        return (PAGED && lane < nch_v && n0 < len) ? p.pt[(int64_t)b * p.pt_sb + (n0 >> p.page_shift)] : -1;
+        return (PAGED && lane < nch && n0 < len) ? p.pt[(int64_t)b * p.pt_sb + (n0 >> p.page_shift)] : -1;
       };
       int cur_pg = PAGED ? fetch_page(t0) : -1;
       const uint64_t t_start = global_ns();
-      long long c_idle = 0;
       int i = 0;
       bool failed = false;
       while (i < NT) {
         int go = 1;
-        if (i >= nst && lane == 0) {
-          go = mbar_try_wait(&empty_ring[i % nst], ((i / nst) & 1) ^ 1);
+        if (i >= ST && lane == 0) {
+          go = mbar_try_wait(&empty_ring[i % ST], ((i / ST) & 1) ^ 1);
           if (!go) {
-            const long long c0 = cstat ? clock64() : 0;
-            go = mbar_try_wait_hint(&empty_ring[i % nst], ((i / nst) & 1) ^ 1, 20000u);
-            if (cstat) c_idle += clock64() - c0;
+            go = mbar_try_wait_hint(&empty_ring[i % ST], ((i / ST) & 1) ^ 1, 20000u);
             if (!go && *abort) go = -1;
             else if (!go && global_ns() - t_start > 2000000000ull) go = -2;
           }
@@ -428,154 +343,148 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         if (!go) continue;
-        const int s = i % nst;
-        if (lane == 0) {
-          if (is_k) TV_TRACE(0, i);
-          if (rank == 0) mbar_arrive_expect_tx(&full_ring[s], TILE);   // both CTAs' bytes
-        }
+        const int s = i % ST;
+        if (lane == 0) mbar_arrive_expect_tx(&full_ring[s], TILE);
         const int pg_now = cur_pg;
         if (PAGED && i + 1 < NT) cur_pg = fetch_page(t0 + i + 1);
         __syncwarp();
         // At most 32 boxes per tile (chunks of >= 8 tokens): one per lane.
         const int bx = (lane - ((i * nb) & 31)) & 31;
-        int c, half;
-        if (is_k || !PAIR) {
-          c = bx >> 1;
-          half = bx & 1;
-        } else {
-          c = bx;
-          half = (int)rank;
-        }
-        const int cc = (ch0 + c) & 31;
-        const int id = __shfl_sync(0xffffffffu, pg_now, cc);   // whole warp: page id of chunk cc
+        const int c = WIDE ? bx : bx >> 1;
+        const int half = WIDE ? 0 : bx & 1;
+        const int id = __shfl_sync(0xffffffffu, pg_now, c & 31);   // whole warp: page id of chunk c
         if (bx < nb) {
-          const int n0 = (t0 + i) * BN + cc * box;
-          int c1, c2, c3;
-          if (PAGED) {
+          const int n0 = (t0 + i) * BN + c * box;
+          uint8_t* dst = base + s * TILE + row_off<WIDE>(c * box, half);
+          if (WIDE) {
+            // 5-D map {64 dims, 8 tokens, 2 halves, page / 8, page * Hkv + head}
             const int off = n0 & ((1 << p.page_shift) - 1);
-            c1 = tok_first ? off : hk;
-            c2 = tok_first ? hk : off;
-            c3 = (id >= 0 && id < p.num_pages) ? id : p.num_pages;   // missing page / past the end: zeros
+            const int ph = (id >= 0 && id < p.num_pages) ? id * p.Hkv + hk : p.num_pages * p.Hkv;
+            tma_load_5d(dst, map, &full_ring[s], 0, 0, 0, off >> 3, ph);
           } else {
-            c1 = tok_first ? n0 : hk;
-            c2 = tok_first ? hk : n0;
-            c3 = b;
+            int c1, c2, c3;
+            if (PAGED) {
+              const int off = n0 & ((1 << p.page_shift) - 1);
+              c1 = tok_first ? off : hk;
+              c2 = tok_first ? hk : off;
+              c3 = (id >= 0 && id < p.num_pages) ? id : p.num_pages;   // missing page / past the end: zeros
+            } else {
+              c1 = tok_first ? n0 : hk;
+              c2 = tok_first ? hk : n0;
+              c3 = b;
+            }
+            tma_load_4d(dst, map, &full_ring[s], half * 64, c1, c2, c3);
           }
-          uint8_t* dst = base + s * slot_bytes + c * box * 128;
-          if (is_k) dst += half * C::KSUB;
-          else if (!PAIR) dst += half * SUB;
-          if (PAIR) tma_load_4d_pair(dst, map, mapa_shared(&full_ring[s], 0), half * 64, c1, c2, c3);
-          else tma_load_4d(dst, map, &full_ring[s], half * 64, c1, c2, c3);
         }
         ++i;
       }
       if (lane == 0) {
-        if (failed) raise_abort<PAIR>(bars, err, 1);
-        if (cstat) cstat[is_k ? 3 : 6] = c_idle;
-        if (*abort && !PAIR) {
+        if (failed) raise_abort(bars, err, 1);
+        if (*abort) {
           // Let this CTA's loads in flight land before shared memory is released.
           volatile int keep_waiting = 0;
-          for (int j = i > nst ? i - nst : 0; j < i; ++j)
-            mbar_wait(&full_ring[j % nst], (j / nst) & 1, &keep_waiting, 200000000ull);
+          for (int j = i > ST ? i - ST : 0; j < i; ++j)
+            mbar_wait(&full_ring[j % ST], (j / ST) & 1, &keep_waiting, 200000000ull);
         }
       }
     }
   } else if (warp == 1 || warp == 11) {
     // ---------------------------------------------------------------- MMA issuers
-    // Two threads (of the pair's first CTA) feed the tensor pipe: warp 11
-    // issues S(j) = Q K^T as soon as K(j) has landed and the softmax warps
-    // have read S(j-2) out of its buffer; warp 1 issues O += P(i) V(i) as
-    // soon as P(i) and V(i) are ready.  Each keeps the pipe busy while the
-    // other waits.
-    if (lane == 0 && rank == 0 && NT > 0) {
+    // Two threads feed the tensor pipe: warp 11 issues S(j) = Q K^T as soon
+    // as K(j) has landed and the softmax warps have read S(j-2) out of its
+    // buffer; warp 1 issues O += P(i) V(i) as soon as P(i) and V(i) are
+    // ready.  Each keeps the pipe busy while the other waits.
+    if (lane == 0 && NT > 0) {
       constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-      constexpr uint32_t id_s = idesc_f16(fmt, C::M, BN, 0);
-      constexpr uint32_t id_pv = idesc_f16(fmt, C::M, HD, 1);
-      constexpr uint32_t hi_k = desc_hi(1024);        // 8-row groups 1 KB apart
+      constexpr uint32_t id_s = idesc_f16(fmt, 128, BN, 0);
+      constexpr uint32_t id_pv = idesc_f16(fmt, 128, HD, 1);
+      constexpr uint32_t hi_q = desc_hi(1024);                 // Q: 8-row groups 1 KB apart
+      constexpr uint32_t hi_kv = desc_hi(WIDE ? 2048 : 1024);  // K / V: 8-row groups
       const uint32_t q_lo = desc_lo(smem_u32(sQ), 16);
       const uint32_t k_lo = desc_lo(smem_u32(sK), 16);
-      const uint32_t v_lo = desc_lo(smem_u32(sV), SUB);   // single CTA: d-halves 16 KB apart
+      // V is MN-major: the leading offset steps between the two 64-dim halves
+      const uint32_t v_lo = desc_lo(smem_u32(sV), WIDE ? 1024 : SUB);
       bool ok = true;
-      long long w_k = 0, w_v = 0, w_p = 0;
-      auto commit = [&](uint64_t* bar) {
-        if (PAIR) tc_commit_pair(bar);
-        else tc_commit(bar);
-      };
       if (warp == 11) {
         for (int j = 0; ok && j < NT; ++j) {
-          const int sb = j % SBUF, ks = j % C::KST;
+          const int sb = j % SBUF, ks = j % ST;
           // buffer sb is free once the softmax warps have read S(j - SBUF)
-          if (j >= SBUF && !(PAIR ? mbar_wait_cluster(&bars->s_free[sb], ((j - SBUF) / SBUF) & 1, abort)
-                                  : mbar_wait(&bars->s_free[sb], ((j - SBUF) / SBUF) & 1, abort))) {
+          if (j >= SBUF && !mbar_wait(&bars->s_free[sb], ((j - SBUF) / SBUF) & 1, abort)) {
             ok = false;
             break;
           }
-          if (!TV_TIMED(w_k, mbar_wait(&bars->k_full[ks], (j / C::KST) & 1, abort))) {
+          if (!mbar_wait(&bars->k_full[ks], (j / ST) & 1, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          TV_TRACE(1, j);
           const uint32_t d = tmem + (uint32_t)(sb * BN);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t qo = (uint32_t)(((kk >> 2) * SUB + (kk & 3) * 32) >> 4);
-            const uint32_t ko = (uint32_t)((ks * C::KSLOT + (kk >> 2) * C::KSUB + (kk & 3) * 32) >> 4);
-            if (PAIR) mma_ss_pair(d, q_lo + qo, hi_k, k_lo + ko, hi_k, id_s, kk > 0 ? 1u : 0u);
-            else mma_ss_w(d, q_lo + qo, hi_k, k_lo + ko, hi_k, id_s, kk > 0 ? 1u : 0u);
+            const uint32_t ko = (uint32_t)((ks * TILE + row_off<WIDE>(0, kk >> 2) + (kk & 3) * 32) >> 4);
+            mma_ss_w(d, q_lo + qo, hi_q, k_lo + ko, hi_kv, id_s, kk > 0 ? 1u : 0u);
           }
-          commit(&bars->s_full[sb]);
-          commit(&bars->k_empty[ks]);
-          TV_TRACE(14, j);
+          tc_commit(&bars->s_full[sb]);
+          tc_commit(&bars->k_empty[ks]);
         }
-        if (!ok) raise_abort<PAIR>(bars, err, 2);
-        if (cstat) cstat[0] = w_k;
+        if (!ok) raise_abort(bars, err, 2);
       } else {
         for (int i = 0; ok && i < NT; ++i) {
-          const int pb = i % PBUF, vs = i % C::VST;
-          const bool got_p = PAIR ? mbar_wait_cluster(&bars->p_full[pb], (i / PBUF) & 1, abort)
-                                  : TV_TIMED(w_p, mbar_wait(&bars->p_full[pb], (i / PBUF) & 1, abort));
-          if (!got_p) {
+          const int pb = i % PBUF, vs = i % ST;
+          if (!mbar_wait(&bars->p_full[pb], (i / PBUF) & 1, abort)) {
             ok = false;
             break;
           }
-          TV_TRACE(2, i);
-          if (!TV_TIMED(w_v, mbar_wait(&bars->v_full[vs], (i / C::VST) & 1, abort))) {
+          if (!mbar_wait(&bars->v_full[vs], (i / ST) & 1, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          if (PAGED) {
+            // A tile ending inside a chunk: the chunk's rows past the last key
+            // came from unused page slots.  Zero them (both halves) before the
+            // PV reads V; chunks starting past the end were zero-filled by TMA.
+            const int r0 = len - (t0 + i) * BN;
+            if (r0 < BN && (r0 % box) != 0) {
+              const int r1 = min(BN, (r0 / box + 1) * box);
+              uint8_t* slot = sV + vs * TILE;
+              for (int n = r0; n < r1; ++n) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  uint4* row = reinterpret_cast<uint4*>(slot + row_off<WIDE>(n, h));
+#pragma unroll
+                  for (int c = 0; c < 8; ++c) row[c] = make_uint4(0u, 0u, 0u, 0u);
+                }
+              }
+              fence_proxy_async();   // generic writes before the MMA's async-proxy reads
+            }
+          }
           const uint32_t a = tmem + P_COL + (uint32_t)(pb * (BN / 2));
 #pragma unroll
           for (int kb = 0; kb < BN / 16; ++kb) {
-            const uint32_t vo = (uint32_t)((vs * C::VSLOT + kb * 2048) >> 4);
+            const uint32_t vo = (uint32_t)((vs * TILE + row_off<WIDE>(16 * kb, 0)) >> 4);
             const uint32_t acc = (i > 0 || kb > 0) ? 1u : 0u;
-            if (PAIR) mma_ts_pair(tmem + O_COL, a + kb * 8, v_lo + vo, hi_k, id_pv, acc);
-            else mma_ts_w(tmem + O_COL, a + kb * 8, v_lo + vo, hi_k, id_pv, acc);
+            mma_ts_w(tmem + O_COL, a + kb * 8, v_lo + vo, hi_kv, id_pv, acc);
           }
-          commit(&bars->v_empty[vs]);
-          commit(&bars->pv_done[pb]);
-          TV_TRACE(3, i);
+          tc_commit(&bars->v_empty[vs]);
+          tc_commit(&bars->pv_done[pb]);
         }
-        if (ok) commit(&bars->o_done);   // tracks every PV; each followed its S
-        else raise_abort<PAIR>(bars, err, 2);
-        if (cstat) {
-          cstat[1] = w_v;
-          cstat[2] = w_p;
-        }
+        if (ok) tc_commit(&bars->o_done);   // tracks every PV; each followed its S
+        else raise_abort(bars, err, 2);
       }
     }
   } else if (warp >= 2 && warp < 10) {
     // ---------------------------------------------------------------- softmax
     // Warps 2-5 take the even tiles, warps 6-9 the odd tiles (tile i in S
     // buffer i % 2), so the two warps sharing a scheduler (and its MUFU unit)
-    // work on successive tiles at the same time.  Warp w covers TMEM lane quarter w % 4: each
-    // thread owns one query row and all 128 keys of its tiles.  The running
-    // reference max passes from tile to tile through shared memory (one
-    // mbarrier phase per tile and quarter); it only moves when a tile's max
-    // exceeds it by more than 2^8, and then O is rescaled before that tile's
-    // PV.  Each warp keeps a partial row sum against the reference it last
-    // saw; the two are combined at the end.
+    // work on successive tiles at the same time.  Warp w covers TMEM lane
+    // quarter w % 4: each thread owns one query row and all 128 keys of its
+    // tiles.  The running reference max passes from tile to tile through
+    // shared memory (one mbarrier phase per tile and quarter); it only moves
+    // when a tile's max exceeds it by more than 2^8, and then O is rescaled
+    // before that tile's PV.  Each warp keeps a partial row sum against the
+    // reference it last saw; the two are combined at the end.
     const int q4 = warp & 3;                      // TMEM lane quarter of this warp
     const int par = (warp - 2) >> 2;              // parity of the tiles this warp takes
     const int rr = q4 * 32 + lane;                // row within the CTA
@@ -591,15 +500,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* pair = &bars->pair[q4];             // both warps of the quarter meet once, at the end
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    long long w_s = 0, w_o = 0;
     for (int i = par; i < NT; i += 2) {
-      if (!__all_sync(0xffffffffu, TV_TIMED(w_s, mbar_wait(&bars->s_full[i % SBUF], (i / SBUF) & 1, abort)))) {
-        raise_abort<PAIR>(bars, err, 3);
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[i % SBUF], (i / SBUF) & 1, abort))) {
+        raise_abort(bars, err, 3);
         ok = false;
         break;
       }
       tc_fence_after();
-      if (lane == 0 && (warp == 2 || warp == 6)) TV_TRACE(4, i);
       const uint32_t s_addr = lane_base + (uint32_t)((i % SBUF) * BN);
       const int n0 = (t0 + i) * BN;
       // Tiles wholly inside the prefix take the unmasked path; the bitmask is
@@ -631,7 +538,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       float mprev = -INFINITY;
       if (i > 0) {
         if (!__all_sync(0xffffffffu, mbar_wait(ref_bar, (i - 1) & 1, abort))) {
-          raise_abort<PAIR>(bars, err, 6);
+          raise_abort(bars, err, 6);
           ok = false;
           break;
         }
@@ -651,7 +558,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       bars->mref[rr] = m_run;       // reference for tile i+1
       __syncwarp();
       if (lane == 0) mbar_arrive(ref_bar);
-      if (lane == 0 && (warp == 2 || warp == 6)) TV_TRACE(5, i);
       const bool need_o = bump && i > 0;
       if (__any_sync(0xffffffffu, need_o)) {
         // O holds tiles up to i-1 scaled to mprev; PV(i-1) must retire first.
@@ -661,9 +567,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // i-1 and that wait is exact too.  PV(i) waits for p_full below.
         bool got = true;
         if (i >= 2) got = mbar_wait(&bars->pv_done[i % PBUF], ((i - 2) / PBUF) & 1, abort);
-        if (got) got = TV_TIMED(w_o, mbar_wait(&bars->pv_done[(i - 1) % PBUF], ((i - 1) / PBUF) & 1, abort));
+        if (got) got = mbar_wait(&bars->pv_done[(i - 1) % PBUF], ((i - 1) / PBUF) & 1, abort);
         if (!__all_sync(0xffffffffu, got)) {
-          raise_abort<PAIR>(bars, err, 4);
+          raise_abort(bars, err, 4);
           ok = false;
           break;
         }
@@ -692,17 +598,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       // All of S(i) is in registers: its buffer can take S(i + SBUF).
       tc_fence_before();
       __syncwarp();
-      if (lane == 0 && (warp == 2 || warp == 6)) TV_TRACE(15, i);
-      if (lane == 0) {
-        if (PAIR) mbar_arrive_cluster(mapa_shared(&bars->s_free[i % SBUF], 0));
-        else mbar_arrive(&bars->s_free[i % SBUF]);
-      }
+      if (lane == 0) mbar_arrive(&bars->s_free[i % SBUF]);
       // P buffer i % PBUF held P(i - 2), this warp's own previous tile, whose
       // PV was issued right after it, so this wait rarely blocks.  Its phase
       // for tile i - 4 completed before this warp wrote P(i - 2), so the
       // parity wait is exact.
       if (i >= PBUF && !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i % PBUF], ((i - PBUF) / PBUF) & 1, abort))) {
-        raise_abort<PAIR>(bars, err, 7);
+        raise_abort(bars, err, 7);
         ok = false;
         break;
       }
@@ -715,19 +617,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) TV_TRACE(6 + warp - 2, i);
-      if (lane == 0) {
-        if (PAIR) mbar_arrive_cluster(mapa_shared(&bars->p_full[i % PBUF], 0));
-        else mbar_arrive(&bars->p_full[i % PBUF]);
-      }
-    }
-    if (cstat && lane == 0 && warp == 2) {
-      cstat[4] = w_s;
-      cstat[5] = w_o;
+      if (lane == 0) mbar_arrive(&bars->p_full[i % PBUF]);
     }
     // ---- epilogue -------------------------------------------------------------
     if (ok && NT > 0 && !__all_sync(0xffffffffu, mbar_wait(&bars->o_done, 0, abort))) {
-      raise_abort<PAIR>(bars, err, 5);
+      raise_abort(bars, err, 5);
       ok = false;
     }
     tc_fence_after();
@@ -738,7 +632,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bars->xl[par * ROWS + rr] = l_run;
       mbar_arrive(pair);
       if (ok && !__all_sync(0xffffffffu, mbar_wait(pair, 0, abort))) {
-        raise_abort<PAIR>(bars, err, 6);
+        raise_abort(bars, err, 6);
         ok = false;
       }
       const float m2 = bars->xm[(par ^ 1) * ROWS + rr];
@@ -789,27 +683,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       else store_row_stats<T>(p, b, mm, hh, lse);
     }
   }
-#undef TV_TRACE
-#undef TV_TIMED
 
-  if (PAIR && *abort) {
-    // The peer's loads may still be signalling this CTA's barriers: give them
-    // time to land before the pair leaves (abort path only).
-    const uint64_t t_end = global_ns() + 200000ull;
-    while (global_ns() < t_end) {
-    }
-  }
   tc_fence_before();
-  if (PAIR) cluster_sync();
-  else __syncthreads();
+  __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    if (PAIR) tmem_dealloc_pair(tmem, TMEM_COLS);
-    else tmem_dealloc(tmem, TMEM_COLS);
-  }
-  if (cstat && threadIdx.x == 0) {
-    p.trace[1024 + cta_id * 4 + 1] = (long long)global_ns();
-    p.trace[1024 + cta_id * 4 + 3] = clock64();
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -827,13 +706,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return fn;
 }
 
+CUtensorMapDataType map_type(int dtype) {
+  return dtype == TV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
 // 4-D map over a KV tensor: head_dim, then tokens and heads in order of
-// increasing stride, then the batch / page index.  Box = 64 x box_tok rows.
+// increasing stride, then the batch / page index.  Box = 64 x box_tok rows
+// (one 64-dim half of a chunk).
 bool make_map(CUtensorMap* map, int dtype, const void* base, uint64_t ntok, uint64_t nhead, uint64_t nouter,
               int64_t s_tok, int64_t s_head, int64_t s_outer, uint32_t box_tok, bool tok_first) {
   auto enc = encoder();
   if (!enc) return false;
-  const CUtensorMapDataType dt = dtype == TV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[4], strides[3];
   cuuint32_t box[4], estr[4] = {1, 1, 1, 1};
   dims[0] = HD;
@@ -848,23 +731,40 @@ bool make_map(CUtensorMap* map, int dtype, const void* base, uint64_t ntok, uint
   dims[3] = nouter;
   strides[2] = (s_outer > 0 ? s_outer : (int64_t)dims[1] * dims[2] * HD) * 2;
   box[3] = 1;
-  const CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  const CUresult r = enc(map, map_type(dtype), 4, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, bool PAGED, bool PAIR>
+// 5-D map of a paged pool whose page and head indices merge (page stride =
+// heads x head stride): {64 dims, 8 tokens, 2 halves (128 B apart), page / 8
+// token groups, page * heads + head}.  One box = box_tok tokens of one head,
+// both halves, landing as [token / 8][half][token % 8][128 B].
+bool make_wide_map(CUtensorMap* map, int dtype, const void* base, uint64_t page, uint64_t nhead, uint64_t npages,
+                   int64_t s_tok, int64_t s_head, uint32_t box_tok) {
+  auto enc = encoder();
+  if (!enc) return false;
+  cuuint64_t dims[5] = {64, 8, 2, page / 8, npages * nhead};
+  cuuint64_t strides[4] = {(cuuint64_t)s_tok * 2, 128, (cuuint64_t)s_tok * 16, (cuuint64_t)s_head * 2};
+  cuuint32_t box[5] = {64, 8, 2, box_tok / 8, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = enc(map, map_type(dtype), 5, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <typename T, bool PAGED, bool WIDE>
 int launch_t(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, int box, int tok_first,
              cudaStream_t st) {
-  using C = Cfg<PAIR>;
-  auto kern = attn_tc_kernel<T, PAGED, PAIR>;
-  const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), C::SMEM);
+  auto kern = attn_tc_kernel<T, PAGED, WIDE>;
+  const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), SMEM);
   if (rc_smem != TV_OK) return rc_smem;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tc_row_blocks(p.R), p.B * p.Hkv, p.splits);
   cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.dynamicSmemBytes = SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -872,7 +772,7 @@ int launch_t(const AttnParams& p, const CUtensorMap& mk, const CUtensorMap& mv, 
   // cluster they run on one GPC, so on one die, and the second read of every
   // tile stays near (measured ~4 % faster at config 2; clusters over several
   // KV heads leave too few free GPC slots for one wave and halve the speed).
-  attr[0].val.clusterDim.x = (PAIR || (tc_row_blocks(p.R) % 2 == 0)) ? 2 : 1;
+  attr[0].val.clusterDim.x = (tc_row_blocks(p.R) % 2 == 0) ? 2 : 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
@@ -892,36 +792,65 @@ bool tc_supported(int dtype, int D, int R, bool paged, int page_shift) {
 }
 int tc_tile_keys() { return BN; }
 int tc_rows_per_cta() { return ROWS; }
-// CTAs per (batch, KV head): a group of more than 128 rows runs as CTA pairs.
-int tc_row_blocks(int R) {
-  const int n = (R + ROWS - 1) / ROWS;
-  return kUsePairs && n > 1 ? (n + 1) & ~1 : n;
-}
+int tc_row_blocks(int R) { return (R + ROWS - 1) / ROWS; }
 
-int launch_attn_tc(const AttnParams& p, int dtype, int D, cudaStream_t st) {
-  if (D != HD) return TV_ERR_UNSUPPORTED;
+// The K and V tensor maps of a request; `wide` tells which box layout they
+// describe.  kernel bit 7 (128) forces the narrow (half-head) boxes on a
+// paged pool.
+int tc_maps(const AttnParams& p, int dtype, int kernel_bits, CUtensorMap* mk, CUtensorMap* mv, int* box_out,
+            bool* wide) {
   const bool paged = p.pt != nullptr;
-  const bool pair = kUsePairs && tc_row_blocks(p.R) > 1;
   // 16-token boxes (or whole pages of 8): enough boxes per tile to keep
   // every producer lane's load in flight.
   const int box = paged && (1 << p.page_shift) < 16 ? (1 << p.page_shift) : 16;
   const bool tok_first = p.k_sn <= p.k_sh;
   if ((p.v_sn <= p.v_sh) != tok_first) return TV_ERR_UNSUPPORTED;
-  CUtensorMap mk, mv;
-  bool ok;
+  *box_out = box;
+  *wide = false;
   if (paged) {
-    ok = make_map(&mk, dtype, p.k, 1u << p.page_shift, p.Hkv, p.num_pages, p.k_sn, p.k_sh, p.k_sb, box, tok_first) &&
-         make_map(&mv, dtype, p.v, 1u << p.page_shift, p.Hkv, p.num_pages, p.v_sn, p.v_sh, p.v_sb, box, tok_first);
-  } else {
-    ok = make_map(&mk, dtype, p.k, p.num_keys, p.Hkv, p.B, p.k_sn, p.k_sh, p.k_sb, box, tok_first) &&
-         make_map(&mv, dtype, p.v, p.num_keys, p.Hkv, p.B, p.v_sn, p.v_sh, p.v_sb, box, tok_first);
+    const uint64_t page = 1u << p.page_shift;
+    const bool wide_ok = !(kernel_bits & 128) && tok_first && p.k_sb == (int64_t)p.Hkv * p.k_sh &&
+                         p.v_sb == (int64_t)p.Hkv * p.v_sh && (int64_t)p.num_pages * p.Hkv < (1ll << 31) - p.Hkv;
+    if (wide_ok && make_wide_map(mk, dtype, p.k, page, p.Hkv, p.num_pages, p.k_sn, p.k_sh, box) &&
+        make_wide_map(mv, dtype, p.v, page, p.Hkv, p.num_pages, p.v_sn, p.v_sh, box)) {
+      *wide = true;
+      return TV_OK;
+    }
+    if (!make_map(mk, dtype, p.k, page, p.Hkv, p.num_pages, p.k_sn, p.k_sh, p.k_sb, box, tok_first) ||
+        !make_map(mv, dtype, p.v, page, p.Hkv, p.num_pages, p.v_sn, p.v_sh, p.v_sb, box, tok_first))
+      return TV_ERR_UNSUPPORTED;
+    return TV_OK;
   }
-  if (!ok) return TV_ERR_UNSUPPORTED;
-  const int tf = tok_first ? 1 : 0;
-#define TV_LAUNCH(TT, PG) (pair ? launch_t<TT, PG, kUsePairs>(p, mk, mv, box, tf, st) : launch_t<TT, PG, false>(p, mk, mv, box, tf, st))
-  if (dtype == TV_BF16) return paged ? TV_LAUNCH(__nv_bfloat16, true) : TV_LAUNCH(__nv_bfloat16, false);
-  return paged ? TV_LAUNCH(__half, true) : TV_LAUNCH(__half, false);
-#undef TV_LAUNCH
+  if (!make_map(mk, dtype, p.k, p.num_keys, p.Hkv, p.B, p.k_sn, p.k_sh, p.k_sb, box, tok_first) ||
+      !make_map(mv, dtype, p.v, p.num_keys, p.Hkv, p.B, p.v_sn, p.v_sh, p.v_sb, box, tok_first))
+    return TV_ERR_UNSUPPORTED;
+  return TV_OK;
+}
+
+int launch_attn_tc(const AttnParams& p, int dtype, int D, int kernel_bits, cudaStream_t st) {
+  if (D != HD) return TV_ERR_UNSUPPORTED;
+  CUtensorMap mk, mv;
+  int box = 16;
+  bool wide = false;
+  const int rc = tc_maps(p, dtype, kernel_bits, &mk, &mv, &box, &wide);
+  if (rc != TV_OK) return rc;
+  const int tf = p.k_sn <= p.k_sh ? 1 : 0;
+  if (p.pt) {
+    if (wide)
+      return dtype == TV_BF16 ? launch_t<__nv_bfloat16, true, true>(p, mk, mv, box, tf, st)
+                              : launch_t<__half, true, true>(p, mk, mv, box, tf, st);
+    return dtype == TV_BF16 ? launch_t<__nv_bfloat16, true, false>(p, mk, mv, box, tf, st)
+                            : launch_t<__half, true, false>(p, mk, mv, box, tf, st);
+  }
+  return dtype == TV_BF16 ? launch_t<__nv_bfloat16, false, false>(p, mk, mv, box, tf, st)
+                          : launch_t<__half, false, false>(p, mk, mv, box, tf, st);
+}
+
+int attn_tc_wide(const AttnParams& p, int dtype, int kernel_bits) {
+  CUtensorMap mk, mv;
+  int box = 16;
+  bool wide = false;
+  return tc_maps(p, dtype, kernel_bits, &mk, &mv, &box, &wide) == TV_OK && wide ? 1 : 0;
 }
 
 }  // namespace tv

@@ -4,10 +4,14 @@
 //
 // Every value crosses NVLink as an 8-byte word: the fp32 bits in the low
 // half, the step number e in the high half.  An aligned 64-bit store is
-// single-copy atomic, so a reader that sees step >= e in a word also sees
-// that step's value: no flags, no fences.  (System-scope fence + flag pairs,
-// one per block, measured ~15 us per step on B200 even with no peer to wait
-// for; the words double the bytes instead, ~1 us per MB at NVLink rates.)
+// single-copy atomic, so a reader that sees step e in a word also sees that
+// step's value: no flags, no fences.  A reader accepts step e exactly: a word
+// of a later step means a peer that already gave up on this rank (a timed-out
+// wait) has moved on and overwritten the slot, so this rank flags the row
+// (status 8, NaN) instead of merging another step's values.
+// (System-scope fence + flag pairs, one per block, measured ~15 us per step
+// on B200 even with no peer to wait for; the words double the bytes instead,
+// ~1 us per MB at NVLink rates.)
 //
 // Each rank owns one exchange buffer, mapped into every rank's address space
 // (rows = B * H * M query rows, in the attention kernel's row order
@@ -41,8 +45,10 @@
 // wrote in its own step e + 1 kernel (push: the reader's partial; owner mode:
 // the final rows, or the partial that the final rows' owner waited for),
 // which starts after the reader's step e kernel completed.  So two slots need
-// no second handshake.  Waits are bounded (2 s per launch): on expiry the
-// status word gets 8 and the rows affected are NaN.
+// no second handshake -- as long as every wait succeeds.  Waits are bounded
+// (2 s per launch): on expiry the status word gets 8 and the rows affected
+// are NaN; the rank then runs ahead of a lagging peer, which sees the later
+// step's tags and flags its rows the same way.
 #include "attn_epilogue.cuh"
 #include "attn_kernels.cuh"
 #include "common.cuh"
@@ -108,19 +114,22 @@ __device__ __forceinline__ void ll_put4(u64* dst, float4 v, int e) {
 __device__ __forceinline__ void ll_put1(u64* dst, float v, int e) {
   asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(ll_word(v, e)) : "memory");
 }
-// Bounded waits until the words carry step >= e; false once the launch's
-// deadline has passed.
+// Bounded waits until the words carry step e.  False once the launch's
+// deadline has passed, or at once when a word carries a later step (this
+// rank fell behind a peer that timed out on it: step e's values are gone).
 __device__ __forceinline__ bool ll_get4(const u64* src, int e, unsigned long long deadline, float4& v) {
   unsigned it = 0;
   for (;;) {
     u64 a, b, c, d;
     asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(src) : "memory");
     asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(c), "=l"(d) : "l"(src + 2) : "memory");
-    if ((int)(a >> 32) >= e && (int)(b >> 32) >= e && (int)(c >> 32) >= e && (int)(d >> 32) >= e) {
+    const int ta = (int)(a >> 32), tb = (int)(b >> 32), tc = (int)(c >> 32), td = (int)(d >> 32);
+    if (ta == e && tb == e && tc == e && td == e) {
       v = make_float4(__uint_as_float((unsigned)a), __uint_as_float((unsigned)b), __uint_as_float((unsigned)c),
                       __uint_as_float((unsigned)d));
       return true;
     }
+    if (ta > e || tb > e || tc > e || td > e) return false;
     if ((++it & 63u) == 0 && now_ns() > deadline) return false;
   }
 }
@@ -129,10 +138,12 @@ __device__ __forceinline__ bool ll_get1(const u64* src, int e, unsigned long lon
   for (;;) {
     u64 a;
     asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(src) : "memory");
-    if ((int)(a >> 32) >= e) {
+    const int ta = (int)(a >> 32);
+    if (ta == e) {
       v = __uint_as_float((unsigned)a);
       return true;
     }
+    if (ta > e) return false;
     if ((++it & 63u) == 0 && now_ns() > deadline) return false;
   }
 }
@@ -305,6 +316,8 @@ int launch_sharded_combine(const AttnParams& p, int dtype, int D, int world, int
   }
   return check_launch();
 }
+
+int64_t sharded_exchange_bytes(int world, int64_t rows, int D) { return layout(world, rows, D).total; }
 
 }  // namespace tv
 

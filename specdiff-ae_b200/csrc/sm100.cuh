@@ -78,9 +78,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_test_wait(bar, parity)) return true;
-#if defined(TV_SPIN_SLEEP_NS) && TV_SPIN_SLEEP_NS > 0
-    __nanosleep(TV_SPIN_SLEEP_NS);
-#endif
     if ((it & 255u) == 0) {
       if (*abort) return false;
       if (global_ns() - t0 > limit_ns) return false;
@@ -195,134 +192,5 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
   return d;
 }
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-// Three-input maximum (sm_100).
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// 2^x for a pair on the FMA pipe, leaving the MUFU unit to the other lanes of
-// the softmax.  Range reduction x = n + f with n = round(x), f in [-1/2, 1/2]:
-// adding 1.5 * 2^23 rounds x to an integer held in the low mantissa bits, whose
-// shift by 23 is n in the exponent field.  2^f is a degree-3 polynomial fitted
-// here for least maximum relative error on [-1/2, 1/2] (iteratively reweighted
-// least squares, max relative error 7.5e-5, far below the 16-bit rounding of P
-// that follows).  x is clamped to >= -125 so the exponent stays in range; the
-// result is then below 2^-125, i.e. nothing next to the row maximum 2^0.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
-  constexpr float c0 = 0.99992810936f, c1 = 0.69326098561f, c2 = 0.24261054228f, c3 = 0.05517132143f;
-  x.x = fmaxf(x.x, -125.f);
-  x.y = fmaxf(x.y, -125.f);
-  const float2 t = add2(x, make_float2(kMagic, kMagic));
-  const float2 n = sub2(t, make_float2(kMagic, kMagic));
-  const float2 f = sub2(x, n);
-  float2 q = fma2(make_float2(c3, c3), f, make_float2(c2, c2));
-  q = fma2(q, f, make_float2(c1, c1));
-  q = fma2(q, f, make_float2(c0, c0));
-  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
-}
-
-// ---- CTA pairs (cluster of two, cta_group::2) -----------------------------------
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Address of the same shared-memory location in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
-  return r;
-}
-// Every thread of both CTAs arrives; release / acquire at cluster scope.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Arrive (release, cluster scope) on an mbarrier given by its cluster address.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// try_wait with acquire at cluster scope (the phase was completed by arrivals
-// from the peer CTA).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                                  uint64_t limit_ns = 2000000000ull) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (*abort) return false;
-      if (global_ns() - t0 > limit_ns) return false;
-    }
-  }
-}
-// Store a word to the same location in CTA `rank` of the cluster.
-__device__ __forceinline__ void st_cluster_u32(const void* p, uint32_t rank, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(mapa_shared(p, rank)), "r"(v) : "memory");
-}
-// TMA tile load whose completion bytes go to the mbarrier of the pair's first
-// CTA (`bar_cluster`, a cluster address); the data lands in this CTA.
-__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int c0, int c1,
-                                                 int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
-      "%5}], [%6];" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar_cluster)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   (uint32_t)__cvta_generic_to_shared(dst_smem)),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// Arrive on `bar` (same offset) in both CTAs of the pair once every tcgen05
-// operation this thread issued so far is done.
-__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
-          (uint32_t)__cvta_generic_to_shared(bar))
-      : "memory");
-}
-
 }  // namespace sm100
 }  // namespace tv

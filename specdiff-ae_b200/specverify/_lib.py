@@ -103,12 +103,13 @@ _SIGNATURES = {
     "tv_version": (ctypes.c_char_p, []),
     "tv_last_cuda_error": (ctypes.c_char_p, []),
     "tv_attn_workspace_size": (c_i32, [ctypes.POINTER(AttnArgs), ctypes.POINTER(c_size)]),
+    "tv_attn_describe": (c_i32, [ctypes.POINTER(AttnArgs), ctypes.POINTER(c_i32)]),
     "tv_verify_attn": (c_i32, [ctypes.POINTER(AttnArgs), c_vp]),
     "tv_verify_attn_static": (c_i32, [ctypes.POINTER(AttnArgs), c_vp]),
     "tv_merge_partials": (c_i32, [c_i32, c_i64, c_i32, c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_vp, c_vp]),
     "tv_sharded_exchange_bytes": (c_i32, [c_i32, c_i64, c_i32, ctypes.POINTER(c_i64)]),
     "tv_verify_attn_sharded_workspace_size": (c_i32, [ctypes.POINTER(AttnArgs), ctypes.POINTER(c_size)]),
-    "tv_verify_attn_sharded": (c_i32, [ctypes.POINTER(AttnArgs), c_i32, c_i32, ctypes.POINTER(c_vp), c_vp]),
+    "tv_verify_attn_sharded": (c_i32, [ctypes.POINTER(AttnArgs), c_i32, c_i32, ctypes.POINTER(c_vp), c_i64, c_vp]),
     "tv_pack_mask": (c_i32, [c_i32, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_i64, c_i64, c_vp]),
     "tv_accept_workspace_size": (c_i32, [ctypes.POINTER(AcceptArgs), ctypes.POINTER(c_size)]),
     "tv_accept": (c_i32, [ctypes.POINTER(AcceptArgs), c_vp]),

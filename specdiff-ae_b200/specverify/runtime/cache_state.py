@@ -26,7 +26,12 @@ class KVCache:
 
     @property
     def shape(self):
-        return (self.data.shape[0], self.data.shape[1], self.current_length.item(), self.data.shape[3])
+        # current_length is one element of the CPU int64 length tensor that
+        # initialize_past_key_values makes (cache_state.py:124-125): reading
+        # it is a host memory load, not a device synchronisation.  It is read
+        # at every use rather than mirrored, because callers update the shared
+        # length tensor directly (verify_new's current_length_data.fill_).
+        return (self.data.shape[0], self.data.shape[1], int(self.current_length), self.data.shape[3])
 
     def copy(self, indices: torch.Tensor, prev_length: int, dim: int = 2):
         tgt = self.data.index_select(dim, indices)

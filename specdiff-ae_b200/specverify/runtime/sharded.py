@@ -27,6 +27,7 @@ max-reduce first: two collectives.
 from __future__ import annotations
 
 import ctypes
+import warnings
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -103,6 +104,7 @@ class PeerExchange:
         nbytes = ctypes.c_int64(0)
         _lib.check(lib.tv_sharded_exchange_bytes(self.world, rows, d, ctypes.byref(nbytes)),
                    "tv_sharded_exchange_bytes")
+        self.nbytes = nbytes.value
         self.buf = symm.empty(-(-nbytes.value // 4), dtype=torch.int32, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
@@ -121,7 +123,7 @@ class PeerExchange:
             self._ws = torch.empty(max(need.value, 256), dtype=torch.uint8, device=device)
         a.workspace = self._ws.data_ptr()
         a.workspace_bytes = self._ws.numel()
-        _lib.check(lib.tv_verify_attn_sharded(ctypes.byref(a), self.world, self.rank, self.bases,
+        _lib.check(lib.tv_verify_attn_sharded(ctypes.byref(a), self.world, self.rank, self.bases, self.nbytes,
                                               _lib.stream_ptr(device)), "tv_verify_attn_sharded")
 
 
@@ -140,7 +142,8 @@ class SequenceShardedVerify:
                  exchange: str = "auto", peer_mode: str = "auto"):
         """``exchange``: ``"peer"`` (NVLink peer memory, kernels only),
         ``"nccl"`` (one all_gather), or ``"auto"`` (peer when the default
-        CUDA partial and merge are used and peer mapping succeeds).
+        CUDA partial and merge are used and peer mapping succeeds; a failed
+        mapping warns, records ``fallback_reason`` and uses the all_gather).
         ``peer_mode`` (peer exchange): ``"push"`` (every rank's partial to
         every peer, one hop), ``"owner"`` (each row block's partials to the
         rank owning it, which hands the final rows back: two hops, less
@@ -157,6 +160,7 @@ class SequenceShardedVerify:
         self.exchange = exchange
         self._bufs = {}
         self._peer = {}
+        self.fallback_reason = None    # set when exchange="auto" fell back to NCCL
 
     def _peer_exchange(self, b, m, h, d, device):
         if self.exchange == "nccl" or (self.exchange == "auto" and (self.partial_fn != self._cuda_partial
@@ -166,10 +170,14 @@ class SequenceShardedVerify:
         if key not in self._peer:
             try:
                 self._peer[key] = PeerExchange(self.group, b * m * h, d, device)
-            except Exception:
+            except Exception as exc:
                 if self.exchange == "peer":
                     raise
-                self._peer[key] = None     # peer mapping unavailable: the all_gather path
+                # exchange="auto": the NCCL all_gather path takes over, and says so
+                warnings.warn(f"SequenceShardedVerify: NVLink peer mapping failed ({type(exc).__name__}: {exc}); "
+                              f"using the NCCL all_gather exchange", RuntimeWarning, stacklevel=3)
+                self.fallback_reason = f"{type(exc).__name__}: {exc}"
+                self._peer[key] = None
         return self._peer[key]
 
     def buffers(self, b, m, h, d, device):

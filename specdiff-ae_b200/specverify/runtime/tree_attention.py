@@ -46,6 +46,7 @@ __all__ = [
     "tree_attention_forward",
     "verify_attention",
     "attention",
+    "describe_attention",
     "pack_tree_mask",
 ]
 
@@ -156,6 +157,17 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         a.workspace_bytes = need.value
     _lib.check(lib.tv_verify_attn(ctypes.byref(a), _lib.stream_ptr(out.device)), "tv_verify_attn")
     return out
+
+
+def describe_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, **kw) -> dict:
+    """The plan :func:`attention` would run for the same arguments (host only):
+    ``kernel`` ("tcgen05" or "warp-mma"), ``splits`` (key splits), ``wide``
+    (tcgen05 loads whole-head TMA boxes) and ``split_p`` (warp-MMA hi+lo P)."""
+    a, _ = attn_args(q, k, v, **kw)
+    info = (ctypes.c_int32 * 4)()
+    _lib.check(_lib.load().tv_attn_describe(ctypes.byref(a), info), "tv_attn_describe")
+    return {"kernel": {2: "tcgen05", 1: "warp-mma"}.get(info[0], "none"), "splits": info[1],
+            "wide": bool(info[2]), "split_p": bool(info[3])}
 
 
 def attn_args(q, k, v, *, num_keys=None, kv_lens=None, page_table=None, mask_bits=None, mask_len=0, out=None,

@@ -193,3 +193,61 @@ def acceptance(*, nodes: int = 64, per_depth: int = 8, vocab: int = VOCAB, prefi
             prev = i + 1
     pos = torch.cat([torch.tensor([prefix_len]), prefix_len + 1 + tree.depth])
     return Acceptance(logits, draft.to(device), tree.parent.to(device), pos.to(device), tree, chain)
+
+
+@dataclass
+class Config1:
+    """BASELINE config 1 (the CPU-runnable single-layer verify), fp32 on the CPU.
+
+    Prefix keys/values in the reference cache layout ``[B, Hkv, S, D]``; the
+    M = 65 tree rows are the root (the last accepted token, position S: the
+    reference's loop keeps ``past_key_values[0][0].shape[2] == draft_position_ids[0]``,
+    ``diffspec_model.py:637``) and 64 drafted nodes at positions S + 1 + depth
+    (``diffspec_model.py:620-624``).  ``q_raw`` / ``k_tree_raw`` are the
+    projections before RoPE; the tree's values need none."""
+    q_raw: torch.Tensor          # [1, M, H, D]
+    k_prefix: torch.Tensor       # [1, Hkv, S, D]
+    v_prefix: torch.Tensor
+    k_tree_raw: torch.Tensor     # [1, Hkv, M, D]
+    v_tree: torch.Tensor
+    positions: torch.Tensor      # [M] int64
+    tree: Tree
+    logits: torch.Tensor         # [M, V] fp32, N(0, 4) (sigma 2)
+    draft: torch.Tensor          # [M] int64 (row 0 = root token)
+    planted: list                # drafted nodes of the planted root-to-leaf chain
+
+    @property
+    def prefix_len(self) -> int:
+        return self.k_prefix.shape[2]
+
+
+def config1(*, seed: int = 0, prefix_len: int = 4096, nodes: int = 64, per_depth: int = 8,
+            heads: int = HEADS, kv_heads: int = KV_HEADS, head_dim: int = HEAD_DIM, vocab: int = VOCAB) -> Config1:
+    """Seeded config-1 inputs (one CPU generator, draws in a fixed order):
+    tree parents, q ~ N(0,1)/sqrt(D), prefix K, V ~ N(0,1), tree K, V ~ N(0,1),
+    logits ~ N(0, 4) over the vocabulary, draft ids ~ U[0, V), then the planted
+    chain (draft id of each chain node = its parent row's argmax)."""
+    gen = torch.Generator().manual_seed(seed)
+    tree = make_tree(gen, nodes, per_depth, root=True)
+    m = tree.rows
+    q = torch.randn((1, m, heads, head_dim), generator=gen) / math.sqrt(head_dim)
+    kp = torch.randn((1, kv_heads, prefix_len, head_dim), generator=gen)
+    vp = torch.randn((1, kv_heads, prefix_len, head_dim), generator=gen)
+    kt = torch.randn((1, kv_heads, m, head_dim), generator=gen)
+    vt = torch.randn((1, kv_heads, m, head_dim), generator=gen)
+    logits = torch.randn((m, vocab), generator=gen) * 2.0
+    draft = torch.randint(0, vocab, (m,), generator=gen)
+    leaf = nodes - 1 - int(torch.randint(0, per_depth, (1,), generator=gen))
+    chain = []
+    p = leaf
+    while p >= 0:
+        chain.append(p)
+        p = int(tree.parent[p])
+    chain.reverse()
+    am = torch.argmax(logits, dim=-1)
+    prev = 0
+    for i in chain:
+        draft[i + 1] = am[prev]
+        prev = i + 1
+    pos = torch.cat([torch.tensor([prefix_len]), prefix_len + 1 + tree.depth])
+    return Config1(q, kp, vp, kt, vt, pos, tree, logits, draft, chain)

@@ -40,7 +40,12 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_python_binding_covers_the_header(lib):
     from specverify import _lib
-    assert set(_lib.EXPORTED) >= set(_declared()) - {"tv_debug_set_trace"}
+    assert set(_lib.EXPORTED) >= set(_declared())
+
+
+def test_no_undeclared_debug_entry_points(lib):
+    """The shipped library exports no profiling hooks beyond the header."""
+    assert not hasattr(lib, "tv_debug_set_trace")
 
 
 def test_host_only_calls(lib):
@@ -106,3 +111,41 @@ def test_ctypes_structs_match_the_header(tmp_path):
         assert got[(cname, "size")] == ctypes.sizeof(py), cname
         for fname, _ in py._fields_:
             assert got[(cname, fname)] == getattr(py, fname).offset, f"{cname}.{fname}"
+
+
+def test_sharded_entry_rejects_a_mismatched_exchange_buffer(lib):
+    """tv_verify_attn_sharded checks the exchange buffer's size against the
+    layout of this request's (world, rows, head_dim) on the host and returns
+    TV_ERR_WORKSPACE before any launch (the pointers here are never used)."""
+    import sys
+    sys.path.insert(0, str(ROOT / "specdiff-ae_b200"))
+    from specverify import _lib
+    a = _lib.AttnArgs()
+    a.dtype = 0                       # TV_BF16
+    a.batch, a.rows, a.heads, a.kv_heads, a.head_dim = 1, 64, 32, 8, 128
+    a.scale = 128 ** -0.5
+    fake = 1 << 20                    # 16-byte aligned stand-ins, never dereferenced
+    a.q, a.k, a.v, a.out = fake, fake, fake, fake
+    a.q_sb, a.q_sm, a.q_sh = 64 * 32 * 128, 32 * 128, 128
+    a.k_sb, a.k_sn, a.k_sh = 8 * 16 * 128, 128, 16 * 128
+    a.v_sb, a.v_sn, a.v_sh = a.k_sb, a.k_sn, a.k_sh
+    a.page_table, a.pt_sb, a.page_size, a.num_pages = fake, 4096, 16, 4096
+    a.num_keys = 32768
+    a.o_sb, a.o_sm, a.o_sh = a.q_sb, a.q_sm, a.q_sh
+    f = lib.tv_verify_attn_sharded
+    f.restype = ctypes.c_int32
+    f.argtypes = [ctypes.POINTER(_lib.AttnArgs), ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
+                  ctypes.c_int64, ctypes.c_void_p]
+    n = ctypes.c_int64(0)
+    lib.tv_sharded_exchange_bytes.argtypes = [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
+                                              ctypes.POINTER(ctypes.c_int64)]
+    assert lib.tv_sharded_exchange_bytes(2, 64 * 32, 128, ctypes.byref(n)) == 0
+    bases = (ctypes.c_void_p * 2)(fake, fake + (1 << 16))
+    for wrong in (n.value - 256, n.value + 256, 0):
+        assert f(ctypes.byref(a), 2, 0, bases, wrong, None) == -5, wrong      # TV_ERR_WORKSPACE
+    # a buffer sized for another world size or row count is rejected too
+    other = ctypes.c_int64(0)
+    assert lib.tv_sharded_exchange_bytes(4, 64 * 32, 128, ctypes.byref(other)) == 0
+    assert f(ctypes.byref(a), 2, 0, bases, other.value, None) == -5
+    assert lib.tv_sharded_exchange_bytes(2, 65 * 32, 128, ctypes.byref(other)) == 0
+    assert f(ctypes.byref(a), 2, 0, bases, other.value, None) == -5

@@ -160,22 +160,66 @@ def test_dropin_prefix_and_tree_forward_vs_golden():
     _close(fused, anchor)
 
 
-def test_config2_rows_against_oracle_and_properties():
-    """Full BASELINE config-2 size (S=65536, 64 nodes, paged, bf16): a subset of
-    rows against the CPU oracle, plus split-count invariance over all rows."""
+def _oracle_by_kv_head(q, k, v, keep, s):
+    """``oatt.full_masked_attention`` one KV head at a time (q [1, M, H, D];
+    k / v [N, Hkv, D]) so the full config-2 problem fits in host memory."""
+    hkv = k.shape[1]
+    g = q.shape[2] // hkv
+    outs, lses = [], []
+    for hk in range(hkv):
+        o, l = oatt.full_masked_attention(q[:, :, hk * g:(hk + 1) * g], k[:, hk:hk + 1].permute(1, 0, 2)[None],
+                                          v[:, hk:hk + 1].permute(1, 0, 2)[None], keep, s)
+        outs.append(o)
+        lses.append(l)
+    return torch.cat(outs, 2), torch.cat(lses, 2)
+
+
+@pytest.mark.parametrize("wide", [True, False])
+def test_config2_all_rows_against_oracle(wide):
+    """Full BASELINE config-2 size (S=65536, 64 nodes, paged, bf16, tcgen05
+    path): every row and head against the CPU oracle, in both TMA box
+    layouts, which must agree bit for bit; plus split-count invariance."""
     from specverify import workloads as wl
     from specverify.runtime import verify_attention
+    from specverify.runtime.tree_attention import describe_attention, pack_tree_mask
     w = wl.paged_verify(seed=0)
+    kern = 2 | (0 if wide else 128)
+    plan = describe_attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table,
+                              mask_bits=pack_tree_mask(w.tree.keep.cuda()), mask_len=w.tree.rows, kernel=kern)
+    assert plan["kernel"] == "tcgen05" and plan["wide"] == wide and plan["splits"] > 1, plan
     out, lse = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
-                                return_lse=True)
+                                return_lse=True, kernel=kern)
     k, v = w.contiguous_kv(0)
-    rows = torch.tensor([0, 7, 31, 63])
-    q_sub = w.q[:, rows].cpu()
-    keep_sub = w.tree.keep[rows]
-    ref, ref_lse = oatt.full_masked_attention(q_sub, k.permute(1, 0, 2)[None].cpu(), v.permute(1, 0, 2)[None].cpu(),
-                                              keep_sub, w.prefix_len)
-    _close(out[:, rows], ref)
-    _close(lse[:, rows], ref_lse, atol=1e-3, rtol=1e-4)
+    ref, ref_lse = _oracle_by_kv_head(w.q.cpu(), k.cpu(), v.cpu(), w.tree.keep, w.prefix_len)
+    _close(out, ref)
+    _close(lse, ref_lse, atol=1e-3, rtol=1e-4)
+    other = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
+                             kernel=kern ^ 128)
+    assert torch.equal(other, out)
     one = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
-                           num_splits=1)
+                           num_splits=1, kernel=kern)
     assert (one.float() - out.float()).abs().max().item() < 2e-3
+
+
+@pytest.mark.parametrize("prefix_len", [65536, 65536 + 7])
+def test_config2_with_root_row_and_poisoned_last_page(prefix_len):
+    """The reference's verify shape prepends the root row (M = 65), so the
+    keys end inside a page (65601 = 4100 pages + 1 token).  The unused slots
+    of the last page hold NaN: the tcgen05 kernel (forced, kernel = 2) must
+    ignore them -- every row against the oracle."""
+    from specverify import workloads as wl
+    from specverify.runtime import verify_attention
+    w = wl.paged_verify(seed=4, root=True, prefix_len=prefix_len)
+    n = w.num_keys
+    assert n % w.page_size != 0
+    last = int(w.page_table[0, n // w.page_size])
+    used = n % w.page_size
+    w.k_pool[last, :, used:] = float("nan")
+    w.v_pool[last, :, used:] = float("nan")
+    out, lse = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
+                                return_lse=True, kernel=2)
+    k, v = w.contiguous_kv(0)
+    assert torch.isfinite(k.float()).all() and torch.isfinite(v.float()).all()   # only valid keys gathered
+    ref, ref_lse = _oracle_by_kv_head(w.q.cpu(), k.cpu(), v.cpu(), w.tree.keep, w.prefix_len)
+    _close(out, ref)
+    _close(lse, ref_lse, atol=1e-3, rtol=1e-4)

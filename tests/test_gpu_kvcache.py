@@ -170,3 +170,45 @@ def test_paged_bundle_verifier_reads_pool_directly():
     ref, ref_lse = oatt.full_masked_attention(q.cpu(), kk[None].cpu(), vv[None].cpu(), mask, 0)
     assert torch.allclose(out.float().cpu(), ref, atol=1e-3, rtol=2e-2)
     assert torch.allclose(lse.cpu(), ref_lse, atol=1e-3)
+
+
+def test_kvcache_length_reads_do_not_synchronise_the_device():
+    """KVCache keeps the reference's CPU length tensor: .shape (read once per
+    layer by the target model) and .cat run with torch's sync debug mode set
+    to error, i.e. without one device synchronisation."""
+    from specverify.runtime import KVCache, initialize_past_key_values
+
+    class _Cfg:
+        num_hidden_layers, num_key_value_heads, hidden_size, num_attention_heads, head_dim = 2, 8, 4096, 32, 128
+
+    class _Attn:
+        def __init__(self):
+            self.q_proj = torch.nn.Linear(1, 1, device="cuda")
+
+    class _Layer:
+        def __init__(self):
+            self.self_attn = _Attn()
+
+    class _Model:
+        config = _Cfg()
+        dtype = torch.bfloat16
+
+        def __init__(self):
+            self.layers = [_Layer(), _Layer()]
+
+    past, data, lengths = initialize_past_key_values(_Model(), 1024)
+    assert lengths.device.type == "cpu" and data[0].is_cuda
+    new = torch.randn(1, 8, 65, 128, device="cuda").bfloat16()
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        for layer in past:
+            k, v = layer
+            assert k.shape[2] == 0
+            ks = k.cat(new)
+            vs = v.cat(new)
+            assert k.shape[2] == 65 and ks.shape[2] == 65 and vs.shape[2] == 65
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    assert isinstance(past[0][0], KVCache)
+    assert torch.equal(data[0][0][:, :, :65].cpu(), new.cpu())

@@ -3,9 +3,10 @@
 Each rank attends its page-aligned shard of a paged prefix (the last rank
 also the tree keys under the bitmask) and the partials are exchanged -- over
 NVLink peer memory (the default) or one NCCL all_gather -- and merged on
-every rank.  The merged output must match the single-GPU kernel on the whole
-cache within bf16 rounding, be identical on every rank and stable over
-repeated steps (the peer path alternates its two buffer slots).
+every rank.  The merged output must meet the 2e-2 / 1e-3 bar against the
+fp32 oracle on the whole cache, match the single-GPU kernel within bf16
+rounding, be identical on every rank and stable over repeated steps (the
+peer path alternates its two buffer slots).
 """
 import datetime
 import os
@@ -57,6 +58,9 @@ def _rank_main(rank, world, port, out_dir):
         attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
                   mask_len=m, out=ref, lse=ref_lse)
         res = {"ref": ref.cpu(), "ref_lse": ref_lse.cpu()}
+        if rank == 0:
+            k, v = w.contiguous_kv(0)
+            res.update(q=w.q.cpu(), k=k.cpu(), v=v.cpu(), keep=w.tree.keep, prefix_len=w.prefix_len)
         for mode in ("peer", "owner", "nccl"):
             ver = sh.SequenceShardedVerify(exchange="nccl" if mode == "nccl" else "peer",
                                            peer_mode="owner" if mode == "owner" else "push")
@@ -78,15 +82,23 @@ def test_sharded_exchanges_match_single_gpu(tmp_path):
                        start_method="spawn")
     r = [torch.load(tmp_path / f"rank{i}.pt") for i in range(world)]
     ref, ref_lse = r[0]["ref"].float(), r[0]["ref_lse"]
+    from oracle import attention as oatt
+    q, k, v = r[0]["q"], r[0]["k"], r[0]["v"]
+    anchor, anchor_lse = oatt.full_masked_attention(q, k.permute(1, 0, 2)[None], v.permute(1, 0, 2)[None],
+                                                    r[0]["keep"], r[0]["prefix_len"])
     for mode in ("peer", "owner", "nccl"):
         first_o, first_l = r[0][mode][0]
         for rank in range(world):
             for o, l in r[rank][mode]:
                 assert torch.equal(o, first_o) and torch.equal(l, first_l), (mode, rank)
         assert torch.isfinite(first_o.float()).all()
-        # two merges of fp32 partials vs the kernel's own split merge: bf16 rounding apart
-        torch.testing.assert_close(first_o.float(), ref, rtol=2e-2, atol=2e-3)
+        # the north star's bar against the fp32 oracle: 2e-2 relative / 1e-3 absolute
+        err = (first_o.float() - anchor).abs()
+        assert bool((err <= 1e-3 + 2e-2 * anchor.abs()).all()), (mode, err.max().item())
+        assert (first_l - anchor_lse).abs().max().item() < 1e-3, mode
+        # and the single-GPU kernel on the whole cache: the same partial algebra
         torch.testing.assert_close(first_l, ref_lse, rtol=1e-5, atol=1e-5)
+        assert (first_o.float() - ref).abs().max().item() < 2e-3
     # both NVLink modes run the same merge in rank order: identical bits
     assert torch.equal(r[0]["peer"][0][0], r[0]["owner"][0][0]) and torch.equal(r[0]["peer"][0][1], r[0]["owner"][0][1])
     # both exchanges merge the same partials with the same algebra
@@ -101,7 +113,7 @@ def _one_gpu_request(prefix_len, seed):
     return w, pack_tree_mask(w.tree.keep.cuda())
 
 
-def _sharded_call(w, bits, bases, world, rank, status=None, num_splits=0, kernel=0):
+def _sharded_call(w, bits, bases, world, rank, status=None, num_splits=0, kernel=0, exchange_bytes=None):
     import ctypes
     from specverify import _lib
     from specverify.runtime.tree_attention import attn_args
@@ -115,8 +127,13 @@ def _sharded_call(w, bits, bases, world, rank, status=None, num_splits=0, kernel
     ws = torch.empty(need.value, dtype=torch.uint8, device="cuda")
     a.workspace, a.workspace_bytes = ws.data_ptr(), need.value
     arr = (ctypes.c_void_p * world)(*bases)
-    _lib.check(lib.tv_verify_attn_sharded(ctypes.byref(a), world, rank, arr, _lib.stream_ptr(out.device)),
-               "tv_verify_attn_sharded")
+    if exchange_bytes is None:
+        n = ctypes.c_int64(0)
+        _lib.check(lib.tv_sharded_exchange_bytes(world, w.q.shape[0] * w.q.shape[1] * w.q.shape[2], w.q.shape[3],
+                                                 ctypes.byref(n)), "exchange bytes")
+        exchange_bytes = n.value
+    _lib.check(lib.tv_verify_attn_sharded(ctypes.byref(a), world, rank, arr, exchange_bytes,
+                                          _lib.stream_ptr(out.device)), "tv_verify_attn_sharded")
     torch.cuda.synchronize()
     return out, lse
 
@@ -180,10 +197,10 @@ def _slot_layout(world, rows, d):
 @pytest.mark.skipif(not cuda_ok(), reason="needs CUDA")
 def test_sharded_entry_exchanges_step_tagged_words():
     """Push mode, rank 0 of 2 on one GPU.  The 'peer' has already posted its
-    partial for every step (words tagged with a large step number, LSE -inf:
-    nothing to add), so the merge must give the one-rank result bit for bit;
-    and rank 0's own partial must have landed in the peer's buffer as words
-    of step 1 (slot 1) whose LSE halves equal the one-rank LSE."""
+    partial for step 1 (words tagged 1 in slot 1, LSE -inf: nothing to add),
+    so the merge must give the one-rank result bit for bit; and rank 0's own
+    partial must have landed in the peer's buffer as words of step 1 (slot 1)
+    whose LSE halves equal the one-rank LSE."""
     from specverify.runtime import attention
     w, bits = _one_gpu_request(1024, seed=7)
     b, m, h, d = w.q.shape
@@ -196,13 +213,12 @@ def test_sharded_entry_exchanges_step_tagged_words():
     L = _slot_layout(2, rows, d)
     mine = _exchange_buffer(2, rows, d)
     peer = _exchange_buffer(2, rows, d)
-    tag = (1 << 30) << 32
+    tag = 1 << 32                                                          # step 1
     words = mine.view(torch.int64)
-    for s in (0, 1):
-        o0 = s * L["slot"] // 8
-        words[o0 + rows * d:o0 + 2 * rows * d] = tag                       # rank 1's O: 0.0
-        l0 = (s * L["slot"] + L["lse"]) // 8
-        words[l0 + rows:l0 + 2 * rows] = tag | 0xFF800000                  # rank 1's LSE: -inf
+    o0 = L["slot"] // 8                                                    # step 1 uses slot 1
+    words[o0 + rows * d:o0 + 2 * rows * d] = tag                           # rank 1's O: 0.0
+    l0 = (L["slot"] + L["lse"]) // 8
+    words[l0 + rows:l0 + 2 * rows] = tag | 0xFF800000                      # rank 1's LSE: -inf
     out, lse = _sharded_call(w, bits, [mine.data_ptr(), peer.data_ptr()], 2, 0, kernel=64)
     assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
     pw = peer.view(torch.int64)
@@ -214,3 +230,34 @@ def test_sharded_entry_exchanges_step_tagged_words():
     # the kernel's row order: (b, kv head, node, group member)
     want = ref_lse.view(b, m, hkv, h // hkv).permute(0, 2, 1, 3).reshape(-1)
     assert torch.equal(lo, want)
+
+
+@pytest.mark.skipif(not cuda_ok(), reason="needs CUDA")
+def test_sharded_entry_lagging_rank_flags_overwritten_words():
+    """Push mode, two ranks emulated on one GPU with two local buffers, run
+    one after the other.  Rank 0 runs three steps while rank 1 runs none:
+    every wait of rank 0 times out (status 8, NaN), and its step-3 partial
+    overwrites slot 1 in rank 1's buffer.  When rank 1 then runs its step 1
+    (slot 1), the words carry step 3: it must flag its rows (status 8, NaN)
+    at once instead of merging step 3's values as step 1's."""
+    w, bits = _one_gpu_request(1024, seed=8)
+    b, m, h, d = w.q.shape
+    rows = b * m * h
+    buf0 = _exchange_buffer(2, rows, d)
+    buf1 = _exchange_buffer(2, rows, d)
+    bases = [buf0.data_ptr(), buf1.data_ptr()]
+    for step in range(3):
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        out, _ = _sharded_call(w, bits, bases, 2, 0, status=status, kernel=64)
+        assert int(status.item()) == 8 and torch.isnan(out.float()).all(), step
+    L = _slot_layout(2, rows, d)
+    tags = buf1.view(torch.int64)[L["slot"] // 8:L["slot"] // 8 + rows * d] >> 32
+    assert bool((tags == 3).all())                     # rank 0's step-3 words sit in slot 1
+    import time
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.perf_counter()
+    out, lse = _sharded_call(w, bits, bases, 2, 1, status=status, kernel=64)
+    elapsed = time.perf_counter() - t0
+    assert int(status.item()) == 8
+    assert torch.isnan(out.float()).all() and torch.isnan(lse).all()
+    assert elapsed < 1.5, f"the later step should be seen at once, not after the 2 s deadline ({elapsed:.2f} s)"

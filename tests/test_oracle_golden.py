@@ -273,3 +273,42 @@ def test_retrieval_oracle_matches_reference():
         for li in range(int(z[p + "layers"])):
             np.testing.assert_array_equal(retrieval.gather(z[p + f"full_k{li}"], idx), z[p + f"work_k{li}"])
             np.testing.assert_array_equal(retrieval.gather(z[p + f"full_v{li}"], idx), z[p + f"work_v{li}"])
+
+
+def test_config1_oracle_matches_reference():
+    """BASELINE config 1 at full size (S = 4096, 65 rows, 32 / 8 heads,
+    vocabulary 128256, seed 0): the seeded inputs reproduce the fixture's
+    checksums; the oracle's verify layer equals the reference's prefix + tree
+    + merge output, its full-softmax anchor agrees to fp32 rounding, and its
+    greedy acceptance and compaction equal ``verify_new``'s."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "specdiff-ae_b200"))
+    from specverify import workloads as wl
+    z = load_golden("config1.npz")
+    c = wl.config1(seed=0)
+    for k in ("q_raw", "k_prefix", "v_prefix", "k_tree_raw", "v_tree", "logits"):
+        assert abs(getattr(c, k).double().sum().item() - float(z[f"sum_{k}"])) < 1e-6, k
+    q = torch.from_numpy(z["q"])
+    kt = torch.from_numpy(z["k_tree"])
+    merged = torch.from_numpy(z["merged"])
+    out = attention.reference_verify_layer(q, c.k_prefix, c.v_prefix, kt, c.v_tree, c.tree.keep)
+    assert (out - merged).abs().max().item() < 1e-6
+    s = c.prefix_len
+    anchor, _ = attention.full_masked_attention(q, torch.cat([c.k_prefix, kt], 2), torch.cat([c.v_prefix, c.v_tree], 2),
+                                                c.tree.keep, s)
+    assert (anchor - merged).abs().max().item() < 1e-5
+    res = acceptance.accept_greedy(c.logits.numpy(), c.draft.numpy(), c.tree.parent.numpy(), c.positions.numpy(), 8)
+    assert res["best_candidate"] == list(z["best_candidate"])
+    assert res["accept_length"] == int(z["accept_length"])
+    assert res["next_token"] == int(z["next_token"])
+    m = c.tree.rows
+    kv = np.zeros((2, 1, 8, s + m + 8, 128), dtype=np.float32)
+    kv[0, :, :, :s] = c.k_prefix[0].numpy()
+    kv[1, :, :, :s] = c.v_prefix[0].numpy()
+    kv[0, :, :, s:s + m] = kt[0].numpy()
+    kv[1, :, :, s:s + m] = c.v_tree[0].numpy()
+    new_len = acceptance.compact_contiguous([kv], s + m, m, res["path"])
+    assert new_len == int(z["new_len"])
+    n = res["accept_length"] + 1
+    assert np.array_equal(kv[:, :, :, s:s + n], z["kv_rows"])

@@ -27,10 +27,10 @@ def _static_entry():
         lib.tv_verify_attn = orig
 
 
-def _case(seed=0):
+def _case(seed=0, device=0):
     from specverify import workloads as wl
     from specverify.runtime import pack_tree_mask
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", device)
     w = wl.paged_verify(prefix_len=8192, nodes=64, per_depth=8, seed=seed, device=dev)
     bits = pack_tree_mask(w.tree.keep.to(dev))
     return w, bits
@@ -73,3 +73,19 @@ def test_static_scratch_uses_splits_and_rejects_oversize():
     assert e.value.status == -5   # TV_ERR_WORKSPACE
     torch.cuda.synchronize()
     assert torch.equal(out, ref_out)
+
+
+@pytest.mark.skipif(not cuda_ok() or torch.cuda.device_count() < 2, reason="needs two CUDA devices")
+def test_static_scratch_on_a_second_device():
+    """The array's address is resolved per device, with that device current:
+    on device 1 the static entry must use device 1's copy of the array and
+    match the workspace entry there, twice in a row."""
+    with torch.cuda.device(1):
+        w, bits = _case(seed=2, device=1)
+        ref_out, ref_lse = _run(w, bits)
+        with _static_entry():
+            out1, lse1 = _run(w, bits)
+            out2, lse2 = _run(w, bits)
+        torch.cuda.synchronize(1)
+    assert torch.equal(out1, ref_out) and torch.equal(lse1, ref_lse)
+    assert torch.equal(out2, ref_out) and torch.equal(lse2, ref_lse)
