@@ -627,6 +627,359 @@ def run_reference(args, rank, world):
     }
 
 
+def _max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_config4(args, rank, world, dev):
+    """one verify step of all 32 layers over a 131072-token
+    paged context with a 128-node depth-10 tree, the context sharded by
+    sequence over the ranks (contiguous, page-aligned shards).
+
+    Each rank allocates only its own shard's pages (and, on the last rank,
+    the tree's pages) of every layer, so per-rank memory falls as 1/N.  A
+    step runs the 32 layers in order -- layer l + 1's queries depend on layer
+    l's output in a real forward pass, so nothing is overlapped across
+    layers: per layer, the verify kernel on the shard, then one kernel that
+    exchanges the partials over NVLink and merges them.  The 32-layer step is
+    one CUDA graph; time = max over ranks.  Also timed: the same step with
+    attention only (each rank's shard, no exchange), which splits the step
+    into attention and exchange + merge, and (N >= 2) both exchange modes."""
+    from specverify import workloads as wl
+    from specverify.runtime import attention, pack_tree_mask
+    from specverify.runtime import sharded as sh
+    from specverify.runtime.tree_attention import describe_attention
+    layers, ctx, nodes, per_depth, page = 32, 131072, 128, 13, 16
+    h, hkv, d = wl.HEADS, wl.KV_HEADS, wl.HEAD_DIM
+    gen = torch.Generator().manual_seed(4)
+    tree = wl.make_tree(gen, nodes, per_depth, root=False)
+    m = tree.rows
+    bits = pack_tree_mask(tree.keep.to(dev))
+    n_prefix_pages = ctx // page
+    tree_pages = -(-m // page)
+    lo, hi = sh.shard_bounds(n_prefix_pages, world, rank)
+    last = rank == world - 1
+    own = (hi - lo) + (tree_pages if last else 0)
+    shard_len = (hi - lo) * page + (m if last else 0)
+    dgen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    pools, tables, qs = [], [], []
+    for layer in range(layers):
+        kp = torch.randn((own, hkv, page, d), generator=dgen, device=dev, dtype=torch.bfloat16)
+        vp = torch.randn((own, hkv, page, d), generator=dgen, device=dev, dtype=torch.bfloat16)
+        perm = torch.randperm(own, generator=gen).to(torch.int32)
+        pools.append((kp, vp))
+        tables.append(perm.view(1, own).to(dev))
+        # layer-independent queries (seeded; the same on every rank)
+        qg = torch.Generator().manual_seed(7000 + layer)
+        qs.append((torch.randn((1, m, h, d), generator=qg) / math.sqrt(d)).to(torch.bfloat16).to(dev))
+    outs = [torch.empty((1, m, h, d), dtype=torch.bfloat16, device=dev) for _ in range(layers)]
+    torch.cuda.synchronize()
+
+    per_layer_kv = ctx * hkv * d * 2 * 2 + m * hkv * d * 2 * 2
+    alg_layer = per_layer_kv + 2 * m * h * d * 2 + m * h * 4 + (n_prefix_pages + tree_pages) * 4 + m * 2 * 8
+    alg = layers * alg_layer
+    vis = int(tree.keep.sum())
+    flops = layers * (4 * m * h * d * ctx + 4 * h * d * vis)
+    plan = describe_attention(qs[0], pools[0][0], pools[0][1], num_keys=shard_len, page_table=tables[0],
+                              mask_bits=bits if last else None, mask_len=m if last else 0)
+
+    def attn_only():
+        for layer in range(layers):
+            kp, vp = pools[layer]
+            attention(qs[layer], kp, vp, num_keys=shard_len, page_table=tables[layer],
+                      mask_bits=bits if last else None, mask_len=m if last else 0, out=outs[layer])
+
+    results = {}
+    if world > 1:
+        for mode in ("push", "owner"):
+            ver = sh.SequenceShardedVerify(exchange="peer", peer_mode=mode)
+
+            def step(ver=ver):
+                for layer in range(layers):
+                    kp, vp = pools[layer]
+                    ver(qs[layer], kp, vp, shard_len, bits if last else None, page_table=tables[layer])
+            for _ in range(args.warmup):
+                step()
+            torch.cuda.synchronize()
+            torch.distributed.barrier()
+            results[mode] = _max_over_ranks(_timed_graph_steps([step], args.steps, args.warmup), world, dev)
+    # attention alone on this rank's shard (max over ranks): the exchange's share
+    if world > 1:
+        torch.distributed.barrier()
+    a_ms = _max_over_ranks(_timed_graph_steps([attn_only], args.steps, args.warmup), world, dev)
+    if world == 1:
+        results["single"] = a_ms
+    best_mode = min(results, key=results.get)
+    ms = results[best_mode]
+    hbm, _ = peaks()
+    mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tpeak = float(mp.get("bf16_tflops_sustained", 1400.0))
+    value = alg / (ms * 1e-3) / 1e9
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V, N(0,1)/sqrt(128) queries)",
+        "config": {"workload": f"config4: sequence-sharded verify, {layers} layers x {ctx}-token paged context, "
+                               f"{m}-node depth-10 tree, bf16, B=1, over {world} GPU(s)",
+                   "parallelism": "single GPU" if world == 1 else f"sequence-sharded x{world}",
+                   "exchange": best_mode, "l2": "inputs larger than L2 (537 MB of KV per layer)",
+                   "algorithmic_bytes_per_step": alg, "flops_per_step": flops,
+                   "per_rank_pages_per_layer": own, "plan_rank0": plan if rank == 0 else None,
+                   "launch": "one CUDA graph per 32-layer step"},
+        "latency_ms": round(ms, 4), "us_per_layer": round(ms * 1e3 / layers, 2),
+        "modes_ms": {k: round(v, 4) for k, v in results.items()},
+        "attention_only_ms": round(a_ms, 4),
+        "exchange_and_merge_ms": round(ms - a_ms, 4) if world > 1 else 0.0,
+        "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1), "peak": tpeak, "unit": "TFLOP/s",
+                     "frac": round(tflops / world / tpeak, 4),
+                     "peak_kind": "measured bf16_tflops_sustained (MEASURED_PEAKS.json)" if mp else "fallback",
+                     "hbm_frac": round(value / world / hbm, 4), "traffic": None,
+                     "kernel": "attn_tc_kernel + sharded_combine_kernel per layer"},
+        "gpu_launches": args.steps * layers * 2,
+    }
+
+
+def run_config5(args, rank, world, dev):
+    """bundle verify over a chunk-arena working set.
+
+    Batch of 4 sequences, each a 262144-token context (one layer's K / V) in
+    2048-token chunks; chunk salience ~ U(0, 1); the top 32 chunks of each
+    sequence form its 65536-token arena, followed by the 96 tokens of a
+    96-node depth-8 tree whose leaves are grouped into 8 bundles by their
+    branching ancestor (``BundleScheduler``).  The verify step is
+    ``FusedBundleVerifier`` semantics (one mask over all keys, ones over the
+    shared arena) over the arena.  Two arena forms are timed:
+
+    * zero-copy: the arena is a page table (``tv_gather_page_table`` of the
+      chunks' pages), verified in place in the paged pool
+      (``PagedBundleVerifier.verify_bundle_paged``);
+    * physical: the chunks are copied into a contiguous arena
+      (``tv_arena_gather``, ``ChunkArena``'s layout) and verified there.
+
+    Also timed: the reference's call pattern -- one ``verify_bundle`` call per
+    bundle over that bundle's rows -- against the single call that scores
+    every bundle's rows in one pass over the arena.  With N > 1 the batch's
+    sequences are split over the ranks (no collective: each rank verifies
+    whole sequences; "scaling": strong, total work fixed)."""
+    from specverify.core.bundle_scheduler import BundleScheduler
+    from specverify.core.kv_cache.chunk_arena import arena_page_table
+    from specverify import _lib, workloads as wl
+    from specverify.runtime import FusedBundleVerifier, PagedBundleVerifier
+    batch, ctx, cs, topk, nodes, per_depth, page = 4, 262144, 2048, 32, 96, 12, 16
+    if batch % world:
+        raise SystemExit(f"config5 splits {batch} sequences over the ranks: use 1, 2 or 4 GPUs")
+    h, hkv, d = wl.HEADS, wl.KV_HEADS, wl.HEAD_DIM
+    ppc, nch = cs // page, ctx // cs
+    gen = torch.Generator().manual_seed(5)
+    tree = wl.make_tree(gen, nodes, per_depth, root=False)
+    m = tree.rows
+    parent = tree.parent.tolist()
+    children = {p for p in parent if p >= 0}
+    leaves = [i for i in range(nodes) if i not in children]
+    sched = BundleScheduler(bundle_size=3, max_bundles=8, device="cpu")
+    bundles = sched.schedule_bundles({"leaf_ids": leaves, "parent_map": {i: parent[i] for i in range(nodes)},
+                                      "depth_map": {i: int(tree.depth[i]) for i in range(nodes)}},
+                                     return_tensors=False)
+    arena = topk * cs
+    n = arena + m
+    mask = torch.ones(m, n, dtype=torch.int8)
+    mask[:, arena:] = tree.keep
+    mask = mask.to(dev)
+    # bundle rows: every node on the paths from the bundle's leaves to the root
+    bundle_rows = []
+    for bd in bundles:
+        rows = set()
+        for leaf in bd["leaves"]:
+            c = leaf
+            while c >= 0:
+                rows.add(c)
+                c = parent[c]
+        bundle_rows.append(torch.tensor(sorted(rows), dtype=torch.long, device=dev))
+    per_rank = batch // world
+    seqs = list(range(rank * per_rank, (rank + 1) * per_rank))
+    tree_pages = -(-m // page)
+    # paged pool: this rank's sequences' full contexts, then their tree pages
+    pool_pages = per_rank * (nch * ppc + tree_pages)
+    dgen = torch.Generator(device=dev).manual_seed(50 + rank)
+    pool = torch.empty((1, 2, pool_pages, hkv, page, d), dtype=torch.bfloat16, device=dev)
+    pool.normal_(generator=dgen)
+    perm = torch.randperm(per_rank * nch * ppc, generator=gen).to(torch.int32).view(per_rank, nch * ppc).to(dev)
+    tree_tbl = (per_rank * nch * ppc + torch.arange(per_rank * tree_pages, dtype=torch.int32)).view(
+        per_rank, tree_pages).to(dev)
+    chunk_ids = []
+    for s_ in seqs:
+        sal = torch.rand(nch, generator=torch.Generator().manual_seed(500 + s_))
+        chunk_ids.append(torch.sort(torch.topk(sal, topk).indices)[0].to(torch.int32).to(dev))
+    qg = torch.Generator().manual_seed(77)
+    q_all = (torch.randn((batch, m, h, d), generator=qg) / math.sqrt(d)).to(torch.bfloat16)
+    q = q_all[seqs[0]:seqs[-1] + 1].contiguous().to(dev)
+    # physical variant: contiguous full caches [B, Hkv, ctx, D] gathered from the pool once (untimed)
+    full_k = torch.empty((per_rank, hkv, ctx, d), dtype=torch.bfloat16, device=dev)
+    full_v = torch.empty_like(full_k)
+    for i in range(per_rank):
+        pg = perm[i].long()
+        full_k[i] = pool[0, 0][pg].permute(1, 0, 2, 3).reshape(hkv, ctx, d)
+        full_v[i] = pool[0, 1][pg].permute(1, 0, 2, 3).reshape(hkv, ctx, d)
+    arena_kv = torch.empty((per_rank, 2, hkv, n, d), dtype=torch.bfloat16, device=dev)   # arena + tree rows
+    for i in range(per_rank):
+        tp = tree_tbl[i].long()
+        arena_kv[i, 0, :, arena:] = pool[0, 0][tp].permute(1, 0, 2, 3).reshape(hkv, -1, d)[:, :m]
+        arena_kv[i, 1, :, arena:] = pool[0, 1][tp].permute(1, 0, 2, 3).reshape(hkv, -1, d)[:, :m]
+    copies = [torch.stack([c, torch.arange(topk, dtype=torch.int32, device=dev)], 1).contiguous()
+              for c in chunk_ids]
+    src_k = torch.tensor([full_k[i].data_ptr() for i in range(per_rank)], dtype=torch.int64, device=dev)
+    src_v = torch.tensor([full_v[i].data_ptr() for i in range(per_rank)], dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    es = 2
+    torch.cuda.synchronize()
+    pver = PagedBundleVerifier(bundle_size=3, device="cuda")
+    fver = FusedBundleVerifier(bundle_size=3, device="cuda")
+    k_arena = arena_kv[:, 0].transpose(1, 2)
+    v_arena = arena_kv[:, 1].transpose(1, 2)
+
+    def zero_copy():
+        tbl = torch.cat([torch.stack([arena_page_table(perm[i], chunk_ids[i], ppc) for i in range(per_rank)]),
+                         tree_tbl], dim=1)
+        return pver.verify_bundle_paged(q, pool, tbl, [mask], shared_prefix_len=arena, num_keys=n)
+
+    def gather():
+        for i in range(per_rank):
+            st = lib.tv_arena_gather(1, hkv, src_k[i:i + 1].data_ptr(), src_v[i:i + 1].data_ptr(), ctx * d * es,
+                                     d * es, ctx, arena_kv[i].data_ptr(), 0, hkv * n * d * es, n * d * es, d * es,
+                                     cs, n, copies[i].data_ptr(), topk, _lib.stream_ptr(dev))
+            _lib.check(st, "tv_arena_gather")
+
+    def physical():
+        gather()
+        return fver.verify_bundle(q, k_arena, v_arena, [mask], shared_prefix_len=arena)
+
+    def per_bundle():
+        outs = []
+        tbl = torch.cat([torch.stack([arena_page_table(perm[i], chunk_ids[i], ppc) for i in range(per_rank)]),
+                         tree_tbl], dim=1)
+        for rows in bundle_rows:
+            outs.append(pver.verify_bundle_paged(q[:, rows], pool, tbl, [mask[rows]], shared_prefix_len=arena,
+                                                 num_keys=n))
+        return outs
+
+    # parity of the two arena forms (same keys, same kernel): identical bits
+    o1, l1 = zero_copy()
+    o2, l2 = physical()
+    torch.cuda.synchronize()
+    same = bool(torch.equal(o1, o2) and torch.equal(l1, l2))
+    pb = per_bundle()
+    pb_diff = max(float((o[0].float() - o1[:, rows].float()).abs().max()) for o, rows in zip(pb, bundle_rows))
+    times = {}
+    for name, fn in (("zero_copy", zero_copy), ("physical", physical), ("gather_only", gather),
+                     ("per_bundle_calls", per_bundle)):
+        if world > 1:
+            torch.distributed.barrier()
+        times[name] = _max_over_ranks(_timed_graph_steps([fn], args.steps, args.warmup), world, dev)
+    ms = times["zero_copy"]
+    kv_bytes = batch * n * hkv * d * 2 * es
+    alg = kv_bytes + 2 * batch * m * h * d * es + batch * m * h * 4 + batch * (arena // page + tree_pages) * 4 \
+        + m * ((n + 63) // 64) * 8
+    vis = int(tree.keep.sum())
+    flops = batch * (4 * m * h * d * arena + 4 * h * d * vis)
+    hbm, _ = peaks()
+    value = alg / (ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V, U(0,1) chunk salience)",
+        "config": {"workload": f"config5: bundle verify, batch {batch}, {ctx}-token contexts in {cs}-token chunks, "
+                               f"top-{topk} arena ({arena} tokens) + {m}-node depth-8 tree in {len(bundles)} "
+                               f"bundles, bf16, over {world} GPU(s)",
+                   "parallelism": "single GPU" if world == 1 else f"sequences split over {world} GPUs",
+                   "bundles": [len(r) for r in bundle_rows], "algorithmic_bytes_per_step": alg,
+                   "flops_per_step": flops, "l2": "inputs larger than L2 (1.07 GB of arena KV per step)",
+                   "launch": "one CUDA graph per step"},
+        "arena_forms_ms": {k: round(v, 4) for k, v in times.items()},
+        "zero_copy_equals_physical": same, "per_bundle_vs_single_call_max_abs_diff": round(pb_diff, 6),
+        "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(value / world / hbm, 4), "traffic": None,
+                     "kernel": "attn_tc_kernel + split_combine_kernel (zero-copy arena)",
+                     "tensor_tflops": round(flops / (ms * 1e-3) / 1e12 / world, 1)},
+        "gpu_launches": args.steps * (per_rank + 4),
+    }
+
+
+def run_config3(args):
+    """the speculative decode loop on a random-init
+    Llama-3.1-8B-architecture target (32 layers, hidden 4096, 32 / 8 heads,
+    SwiGLU 14336, vocabulary 128256, RoPE theta 500000, bf16) with a
+    one-layer EAGLE3-shaped draft head, after a 65536-token context, 64-node
+    depth-8 trees, stochastic acceptance at temperature 1.0, seed 0
+    (``specverify.draft.spec_decode``).  The context's K / V are filled with
+    N(0, 1) values in place of a prefill (not part of the decode metric).
+    value = verified tokens per second of the decode loop (wall clock, host
+    reads included).  Replicas only across GPUs: the loop does not shard."""
+    from specverify.draft.spec_decode import SpecDecodeModel
+    from specverify.runtime import attention, pack_tree_mask
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py --workload config3 needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    prompt, new_tokens, nodes, depth = 65536, 512, 64, 8
+    model = SpecDecodeModel.from_config(device=dev, seed=0, max_tokens=prompt + new_tokens + 2 * nodes + 64)
+    model.diffspec_generate(prompt, max_new_tokens=8 * args.warmup, nodes=nodes, max_depth=depth,
+                            temperature=1.0, seed=1, max_steps=args.warmup)           # warm-up
+    torch.cuda.synchronize()
+    r = model.diffspec_generate(prompt, max_new_tokens=new_tokens, nodes=nodes, max_depth=depth, temperature=1.0,
+                                seed=0)
+    tok_s = len(r["tokens"]) / r["wall_s"]
+    steps = r["steps"]
+    ph = r["phases_ms"]
+    step_ms = r["wall_s"] * 1e3 / steps
+    # the verify step's attention alone: 32 layers of the verify kernel at the
+    # loop's shapes (65 rows, ~66K keys), graph-replayed
+    s = model.shape
+    m = nodes + 1
+    start = prompt + new_tokens // 2
+    q = (torch.randn(1, m, s.heads, s.head_dim, device=dev) / math.sqrt(s.head_dim)).to(model.dtype)
+    keep = torch.tril(torch.ones(m, m, dtype=torch.int8, device=dev))
+    bits = pack_tree_mask(keep)
+
+    def layers_attention():
+        for li in range(s.layers):
+            attention(q, model.pool[li, 0], model.pool[li, 1], num_keys=start + m, page_table=model.page_table,
+                      mask_bits=bits, mask_len=m)
+    attn_ms = _timed_graph_steps([layers_attention], 10, 3)
+    weights = sum(t.numel() * t.element_size() for t in
+                  [model.embed, model.lm_head] + [w for L in model.layers for w in (L.wqkv, L.wo, L.wgu, L.wdown)])
+    return {
+        "metric": METRIC, "value": round(tok_s, 2), "unit": "verified tok/s", "n_gpus": 1, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0, 0.02) weights, N(0,1) context K/V, seeded sampling)",
+        "config": {"workload": f"config3: speculative decode loop, random-init Llama-3.1-8B target (32 layers) + "
+                               f"1-layer EAGLE3-shaped draft (draft vocab {s.draft_vocab}, working set "
+                               f"{model.draft_ctx} tokens), {prompt}-token context, {new_tokens} new tokens, "
+                               f"{nodes}-node depth-{depth} trees, temperature 1.0, seed 0",
+                   "parallelism": "single GPU (replicas only across GPUs)",
+                   "launch": "eager loop, one host read per step (the accepted length)"},
+        "tokens": len(r["tokens"]), "accepted_per_step_mean": round(sum(r["accepted_per_step"]) / steps, 4),
+        "phase_ms_per_step": {k.replace("_ms", ""): round(v / steps, 4) for k, v in ph.items()},
+        "verify_attention_ms_per_step": round(attn_ms, 4),
+        "attention_share_of_step": round(attn_ms / step_ms, 4),
+        "target_weight_bytes": weights,
+        "roofline": {"bound": "hbm", "achieved": round((weights + s.layers * start * s.kv_heads * s.head_dim * 4)
+                                                      / (step_ms * 1e-3) / 1e9, 1),
+                     "peak": peaks()[0], "unit": "GB/s", "frac": None, "traffic": None,
+                     "kernel": "whole step: target weights + KV read once per step over the step time",
+                     "note": "frac omitted: the step also runs the draft (8 forwards) and host work"},
+        # per step, this library's kernels: draft 8 x (mask pack, rope + append, attention, split
+        # combine) + tree finalize; target 32 x (rope + append, attention, split combine); lm_head scan +
+        # acceptance; paged compaction
+        "gpu_launches": steps * (8 * 4 + 1 + 32 * 3 + 2 + 1),
+    }
+
+
 _JSON_OUT = sys.stdout
 
 
@@ -975,7 +1328,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the side measurements (root-row variant, reference GPU ops)")
-    ap.add_argument("--workload", choices=["verify", "rope-append", "lmhead-accept", "tree-finalize",
+    ap.add_argument("--workload", choices=["verify", "config3", "config4", "config5", "rope-append", "lmhead-accept", "tree-finalize",
                                            "chunk-retrieve"], default="verify")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1006,6 +1359,10 @@ def main():
         if rank == 0:
             print(json.dumps(run_retrieve(args)), file=_JSON_OUT, flush=True)
         return
+    if args.workload == "config3":
+        if rank == 0:
+            print(json.dumps(run_config3(args)), file=_JSON_OUT, flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
@@ -1020,9 +1377,14 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     try:
-        res = run_ours(args, rank, world, dev)
+        if args.workload == "config4":
+            res = run_config4(args, rank, world, dev)
+        elif args.workload == "config5":
+            res = run_config5(args, rank, world, dev)
+        else:
+            res = run_ours(args, rank, world, dev)
         if rank == 0:
-            if not args.no_cpu_baseline and world == 1:
+            if not args.no_cpu_baseline and world == 1 and args.workload == "verify":
                 gbs, sec, thr, desc = cpu_reference_sample(8192)
                 res["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
                                        "sample": desc + f"; {sec * 1e3:.1f} ms per pass"}

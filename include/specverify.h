@@ -154,6 +154,12 @@ typedef struct tv_attn_args {
   int32_t* status;               /* optional device word, zeroed by the caller;
                                     set nonzero if a kernel had to abandon a
                                     wait (its output rows are then NaN)     */
+  const uint8_t* mask_words_full;/* optional, [batch][mask words] from
+                                    tv_mask_word_summary: 1 where every row's
+                                    mask word is all ones, so the tcgen05
+                                    kernel skips masking key tiles made only
+                                    of such words (same result, less work) */
+  int64_t mask_words_full_sb;
 } tv_attn_args;
 
 int tv_attn_workspace_size(const tv_attn_args* args, size_t* bytes);
@@ -242,6 +248,15 @@ int tv_verify_attn_sharded(const tv_attn_args* args, int32_t world, int32_t rank
 int tv_pack_mask(int32_t kind, const void* src, int64_t s_b, int64_t s_r, int64_t s_c,
                  int32_t batch, int32_t rows, int32_t cols,
                  uint64_t* out, int64_t out_sb, int64_t out_sr, void* stream);
+
+/* Per (batch, 64-key word) of a packed mask [batch][rows][words] (strides
+ * sb, sr in words): out[b * out_sb + w] = 1 when word w is all ones in every
+ * row, else 0.  For tv_attn_args.mask_words_full: a mask that leaves a long
+ * shared prefix visible to every row (bundle verification,
+ * bundle_verifier.py:166-216, masks the whole key range) then costs the
+ * verify kernel nothing there.  No counterpart in the reference. */
+int tv_mask_word_summary(const uint64_t* bits, int32_t batch, int32_t rows, int32_t words, int64_t sb, int64_t sr,
+                         uint8_t* out, int64_t out_sb, void* stream);
 
 /* ---- acceptance --------------------------------------------------------
  * One target token per node, then the acceptance rule of verify_new:

@@ -212,6 +212,8 @@ void fill_params(const tv_attn_args* a, const Plan& pl, bool partials, AttnParam
   p.mask_len = a->mask_len;
   p.mask = a->mask;
   p.mask_sb = a->mask_sb; p.mask_sm = a->mask_sm;
+  p.mfull = a->mask ? a->mask_words_full : nullptr;
+  p.mfull_sb = a->mask_words_full_sb;
   p.B = a->batch; p.M = a->rows; p.H = a->heads; p.Hkv = a->kv_heads;
   p.G = a->heads / a->kv_heads;
   p.R = a->rows * p.G;

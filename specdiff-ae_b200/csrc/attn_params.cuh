@@ -21,6 +21,8 @@ struct AttnParams {
   int mask_len;
   const uint64_t* mask;
   int64_t mask_sb, mask_sm;
+  const uint8_t* mfull;    // optional per (batch, mask word): all rows see all 64 keys
+  int64_t mfull_sb;
   int B, M, H, Hkv, G, R;  // R = M * G query rows per (batch, kv head)
   float scale_log2;        // softmax scale * log2(e)
   int splits;

@@ -510,8 +510,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t s_addr = lane_base + (uint32_t)((i % SBUF) * BN);
       const int n0 = (t0 + i) * BN;
       // Tiles wholly inside the prefix take the unmasked path; the bitmask is
-      // applied only where the tail begins.
-      const bool edge = (n0 + BN > len) || (n0 + BN > tail);
+      // applied only where the tail begins, and not on tiles whose mask words
+      // are all ones in every row (the optional word summary).
+      bool edge = (n0 + BN > len) || (n0 + BN > tail);
+      if (edge && p.mfull && n0 + BN <= len) {
+        const int a0 = n0 > tail ? n0 - tail : 0, e0 = n0 + BN - tail;   // gated keys [a0, e0), e0 <= mlen
+        bool full = true;
+        for (int w = a0 >> 6; w <= (e0 - 1) >> 6; ++w) full = full && p.mfull[(int64_t)b * p.mfull_sb + w] != 0;
+        edge = !full;
+      }
       uint32_t keep[4] = {~0u, ~0u, ~0u, ~0u};
       if (edge) {
 #pragma unroll

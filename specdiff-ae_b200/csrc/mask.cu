@@ -33,10 +33,36 @@ __global__ void __launch_bounds__(256) pack_mask_kernel(int kind, const void* sr
   }
 }
 
+// One thread per (batch, word): AND of the word over all rows.
+__global__ void __launch_bounds__(128) mask_word_summary_kernel(const uint64_t* bits, int rows, int words, int64_t sb,
+                                                                int64_t sr, uint8_t* out, int64_t out_sb) {
+  const int b = blockIdx.y;
+  const int w = blockIdx.x * 128 + threadIdx.x;
+  if (w >= words) return;
+  const uint64_t* col = bits + (int64_t)b * sb + w;
+  uint64_t acc = ~0ull;
+  for (int r = 0; r < rows && acc == ~0ull; ++r) acc &= col[(int64_t)r * sr];
+  out[(int64_t)b * out_sb + w] = acc == ~0ull ? 1 : 0;
+}
+
 }  // namespace
 }  // namespace tv
 
 using namespace tv;
+
+extern "C" int tv_mask_word_summary(const uint64_t* bits, int32_t batch, int32_t rows, int32_t words, int64_t sb,
+                                    int64_t sr, uint8_t* out, int64_t out_sb, void* stream) {
+  if (batch < 0 || rows < 0 || words < 0) return TV_ERR_SHAPE;
+  if (batch == 0 || words == 0) return TV_OK;
+  if (!bits || !out) return TV_ERR_NULL;
+  if (sr < words || (batch > 1 && (sb < sr * rows || out_sb < words))) return TV_ERR_SHAPE;
+  if (batch > 65535) return TV_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(bits) & 7) != 0) return TV_ERR_ALIGN;
+  dim3 grid((words + 127) / 128, batch);
+  mask_word_summary_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(bits, rows, words, sb, sr, out,
+                                                                               out_sb);
+  return check_launch();
+}
 
 extern "C" int tv_pack_mask(int32_t kind, const void* src, int64_t s_b, int64_t s_r, int64_t s_c, int32_t batch,
                             int32_t rows, int32_t cols, uint64_t* out, int64_t out_sb, int64_t out_sr, void* stream) {

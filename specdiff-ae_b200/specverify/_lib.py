@@ -52,6 +52,7 @@ class AttnArgs(ctypes.Structure):
         ("weight", c_vp), ("w_sb", c_i64), ("w_sm", c_i64), ("w_sh", c_i64),
         ("num_splits", c_i32), ("kernel", c_i32),
         ("workspace", c_vp), ("workspace_bytes", c_size), ("status", c_vp),
+        ("mask_words_full", c_vp), ("mask_words_full_sb", c_i64),
     ]
 
 
@@ -111,6 +112,7 @@ _SIGNATURES = {
     "tv_verify_attn_sharded_workspace_size": (c_i32, [ctypes.POINTER(AttnArgs), ctypes.POINTER(c_size)]),
     "tv_verify_attn_sharded": (c_i32, [ctypes.POINTER(AttnArgs), c_i32, c_i32, ctypes.POINTER(c_vp), c_i64, c_vp]),
     "tv_pack_mask": (c_i32, [c_i32, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_i64, c_i64, c_vp]),
+    "tv_mask_word_summary": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "tv_accept_workspace_size": (c_i32, [ctypes.POINTER(AcceptArgs), ctypes.POINTER(c_size)]),
     "tv_accept": (c_i32, [ctypes.POINTER(AcceptArgs), c_vp]),
     "tv_compact_contig": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i32, c_i64, c_vp, c_i32, c_vp]),

@@ -8,7 +8,10 @@ attention runs over all N keys under it, and the result is
 ``(out [B, M, H, D], lse [B, M, H] fp32)``.  The mask is packed to one bit
 per key and the verify-attention kernel scores every node of a KV head in
 one CTA, so each KV tile -- the shared prefix included -- is read from
-memory once per head for all of the bundle's rows.
+memory once per head for all of the bundle's rows.  The mask covers every
+key, as the reference's does; a per-word summary (all rows see all 64 keys)
+lets the kernel skip masking the tiles of a shared prefix every row sees,
+with the same result for any mask.
 
 :class:`PagedBundleVerifier.verify_bundle_paged` is implemented (the
 reference raises ``NotImplementedError``, ``:341-366``): it reads K/V through
@@ -22,7 +25,7 @@ from typing import Dict, List, Tuple
 import torch
 
 from .. import _lib
-from .tree_attention import attention, pack_tree_mask
+from .tree_attention import attention, mask_word_summary, pack_tree_mask
 
 
 class FusedBundleVerifier:
@@ -54,7 +57,8 @@ class FusedBundleVerifier:
         n = k.size(1)
         bits = pack_tree_mask(self._bundle_mask(masks, b).to(q.device), cols=n)
         lse = torch.empty((b, m, h), dtype=torch.float32, device=q.device)
-        out = attention(q, k, v, num_keys=n, mask_bits=bits, mask_len=n, lse=lse)
+        out = attention(q, k, v, num_keys=n, mask_bits=bits, mask_len=n, lse=lse,
+                        mask_full=mask_word_summary(bits))
         return out, lse
 
     def get_statistics(self) -> Dict:
@@ -90,5 +94,5 @@ class PagedBundleVerifier(FusedBundleVerifier):
         bits = pack_tree_mask(mask, cols=n)
         lse = torch.empty((b, m, h), dtype=torch.float32, device=q.device)
         out = attention(q, kv_pages[layer_idx, 0], kv_pages[layer_idx, 1], num_keys=n, page_table=pt,
-                        mask_bits=bits, mask_len=n, lse=lse)
+                        mask_bits=bits, mask_len=n, lse=lse, mask_full=mask_word_summary(bits))
         return out, lse

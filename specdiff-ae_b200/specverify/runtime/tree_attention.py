@@ -47,6 +47,7 @@ __all__ = [
     "verify_attention",
     "attention",
     "describe_attention",
+    "mask_word_summary",
     "pack_tree_mask",
 ]
 
@@ -104,6 +105,20 @@ def pack_tree_mask(mask: torch.Tensor, q_len: Optional[int] = None, batch: Optio
     return out
 
 
+def mask_word_summary(bits: torch.Tensor) -> torch.Tensor:
+    """uint8 ``[B, words]``: 1 where a 64-key word of the packed mask
+    ``[B, M, words]`` is all ones in every row (``tv_mask_word_summary``)."""
+    dev = _lib.require_cuda(bits)
+    if bits.dim() != 3 or bits.dtype != torch.int64 or bits.stride(2) != 1:
+        raise _lib.SpecVerifyError(-1, "bits must be packed int64 [B, M, words] with unit word stride")
+    b, m, words = bits.shape
+    out = torch.empty((b, words), dtype=torch.uint8, device=dev)
+    st = _lib.load().tv_mask_word_summary(bits.data_ptr(), b, m, words, bits.stride(0), bits.stride(1),
+                                          out.data_ptr(), out.stride(0), _lib.stream_ptr(dev))
+    _lib.check(st, "tv_mask_word_summary")
+    return out
+
+
 def _kv_strides(t: torch.Tensor, paged: bool):
     """(sb, sn, sh): contiguous [B, N, Hkv, D] or a paged pool [P, Hkv, page, D]."""
     if t.dim() != 4 or t.stride(3) != 1:
@@ -131,7 +146,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               scale: Optional[float] = None,
               num_splits: int = 0,
               kernel: int = 0,
-              status: Optional[torch.Tensor] = None) -> torch.Tensor:
+              status: Optional[torch.Tensor] = None,
+              mask_full: Optional[torch.Tensor] = None) -> torch.Tensor:
     """General verify attention (see ``tv_verify_attn`` in include/specverify.h).
 
     q: [B, M, H, D]; k/v: contiguous ``[B, N, Hkv, D]`` views, or a paged pool
@@ -141,12 +157,14 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     addressed as ``[b, m, h]`` through the given strides (default: their
     own ``[B, M, H]`` strides).  ``status`` (int32 [1], zeroed by the caller)
     receives a nonzero code if a kernel had to abandon a bounded wait.
+    ``mask_full`` (uint8 ``[B, words]`` from :func:`mask_word_summary`) lets
+    the tcgen05 kernel skip masking key tiles every row fully sees.
     Returns ``out``.
     """
     a, out = attn_args(q, k, v, num_keys=num_keys, kv_lens=kv_lens, page_table=page_table, mask_bits=mask_bits,
                        mask_len=mask_len, out=out, out_f32=out_f32, lse=lse, lse_strides=lse_strides,
                        aux_lse=aux_lse, aux_strides=aux_strides, weight=weight, weight_strides=weight_strides,
-                       scale=scale, num_splits=num_splits, kernel=kernel, status=status)
+                       scale=scale, num_splits=num_splits, kernel=kernel, status=status, mask_full=mask_full)
     lib = _lib.load()
     need = ctypes.c_size_t(0)
     _lib.check(lib.tv_attn_workspace_size(ctypes.byref(a), ctypes.byref(need)), "tv_attn_workspace_size")
@@ -172,11 +190,11 @@ def describe_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, **kw) 
 
 def attn_args(q, k, v, *, num_keys=None, kv_lens=None, page_table=None, mask_bits=None, mask_len=0, out=None,
               out_f32=False, lse=None, lse_strides=None, aux_lse=None, aux_strides=None, weight=None,
-              weight_strides=None, scale=None, num_splits=0, kernel=0, status=None):
+              weight_strides=None, scale=None, num_splits=0, kernel=0, status=None, mask_full=None):
     """The checked ``tv_attn_args`` of an :func:`attention` request (no
     workspace set) and its output tensor (allocated when ``out`` is None).
     The tensors must stay alive while the struct is used."""
-    dev = _lib.require_cuda(q, k, v, page_table, kv_lens, mask_bits, out, lse, aux_lse, weight)
+    dev = _lib.require_cuda(q, k, v, page_table, kv_lens, mask_bits, out, lse, aux_lse, weight, mask_full)
     if q.dim() != 4 or q.stride(3) != 1:
         raise _lib.SpecVerifyError(-3, f"q must be [B, M, H, D] with unit stride on D, got {tuple(q.shape)}")
     b, m, h, d = q.shape
@@ -228,6 +246,11 @@ def attn_args(q, k, v, *, num_keys=None, kv_lens=None, page_table=None, mask_bit
         a.mask = mask_bits.data_ptr()
         a.mask_sb = mask_bits.stride(0) if mask_bits.shape[0] > 1 else 0
         a.mask_sm = mask_bits.stride(1)
+        if mask_full is not None:
+            if mask_full.dtype != torch.uint8 or mask_full.dim() != 2 or mask_full.shape[1] < -(-mask_len // 64):
+                raise _lib.SpecVerifyError(-1, "mask_full must be uint8 [B, words] covering mask_len")
+            a.mask_words_full = mask_full.data_ptr()
+            a.mask_words_full_sb = mask_full.stride(0) if mask_full.shape[0] > 1 else 0
     a.out = out.data_ptr()
     a.o_sb, a.o_sm, a.o_sh = out.stride(0), out.stride(1), out.stride(2)
     if out.stride(3) != 1:

@@ -212,3 +212,46 @@ def test_kvcache_length_reads_do_not_synchronise_the_device():
         torch.cuda.set_sync_debug_mode(0)
     assert isinstance(past[0][0], KVCache)
     assert torch.equal(data[0][0][:, :, :65].cpu(), new.cpu())
+
+
+@pytest.mark.parametrize("holes", [False, True])
+def test_bundle_mask_summary_skips_only_fully_visible_tiles(holes):
+    """Bundle verification masks every key (the reference's contract).  With a
+    16K-token shared prefix every row sees, the tcgen05 kernel skips masking
+    those tiles through the per-word summary -- bit-identical to masking them.
+    With a few hidden prefix keys in some rows (holes), the summary marks
+    those words and the kernel masks them: the result still matches the
+    oracle over the full mask."""
+    from specverify.runtime import PagedBundleVerifier, attention, mask_word_summary, pack_tree_mask
+    from specverify import workloads as wl
+    b, nodes, spl, page = 2, 96, 16384, 16
+    gen = torch.Generator().manual_seed(21)
+    tree = wl.make_tree(gen, nodes, 12, root=False)
+    m = tree.rows
+    n = spl + m
+    mask = torch.ones(m, n, dtype=torch.int8)
+    mask[:, spl:] = tree.keep
+    if holes:
+        mask[3, 5000] = 0
+        mask[40, 129:140] = 0
+        mask[95, 16380] = 0
+    pages = -(-n // page)
+    pool = torch.randn(1, 2, b * pages + 4, 8, page, 128, generator=gen).bfloat16().cuda()
+    table = torch.randperm(b * pages, generator=gen).to(torch.int32).view(b, pages).cuda()
+    q = (torch.randn(b, m, 32, 128, generator=gen) / math.sqrt(128)).bfloat16().cuda()
+    ver = PagedBundleVerifier(device="cuda")
+    out, lse = ver.verify_bundle_paged(q, pool, table, [mask.cuda()], shared_prefix_len=spl, num_keys=n)
+    bits = pack_tree_mask(mask.cuda(), batch=b, cols=n)
+    summary = mask_word_summary(bits)
+    words = summary.cpu()
+    assert bool(words[:, : spl // 64].all()) != holes
+    plain = torch.empty_like(q)
+    attention(q, pool[0, 0], pool[0, 1], num_keys=n, page_table=table, mask_bits=bits, mask_len=n, out=plain,
+              kernel=2)
+    assert torch.equal(out, plain)                     # skipping the mask never changes a bit
+    for s in range(b):
+        kk = pool[0, 0][table[s].long()].permute(1, 0, 2, 3).reshape(8, -1, 128)[:, :n]
+        vv = pool[0, 1][table[s].long()].permute(1, 0, 2, 3).reshape(8, -1, 128)[:, :n]
+        ref, ref_lse = oatt.full_masked_attention(q[s:s + 1].cpu(), kk[None].cpu(), vv[None].cpu(), mask, 0)
+        assert torch.allclose(out[s:s + 1].float().cpu(), ref, atol=1e-3, rtol=2e-2)
+        assert torch.allclose(lse[s:s + 1].cpu(), ref_lse, atol=1e-3)

@@ -1,0 +1,74 @@
+"""The speculative decode loop (``specverify.draft.spec_decode``) on a tiny
+random-init Llama-shaped model: with greedy acceptance, speculative decoding
+must produce exactly the target's own greedy continuation -- the defining
+property of the reference's loop (``diffspec_model.py:268-754``).  The plain
+continuation is decoded one token at a time through the same model (one-row
+verify steps); a step fed the true continuation as a chain must accept all of
+it, and the compacted cache must then continue the same sequence."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import cuda_ok
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ok(), reason="needs a CUDA device")]
+
+PROMPT = 300
+
+
+def _model():
+    from specverify.draft.spec_decode import LlamaShape, SpecDecodeModel
+    shape = LlamaShape(hidden=512, layers=4, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1000,
+                       draft_vocab=1000, feature_layers=(0, 1, 2))
+    m = SpecDecodeModel.from_config(shape, device="cuda", seed=0, max_tokens=1024, draft_ctx=256)
+    # well-separated logits: the argmax cannot flip on rounding differences
+    # between a 1-row and a many-row step
+    m.lm_head.normal_(0.0, 1.0, generator=torch.Generator(device="cuda").manual_seed(9))
+    return m
+
+
+def _plain_greedy(m, root: int, start: int, n: int):
+    """Target greedy decode, one token per step through the same kernels."""
+    from specverify.runtime import pack_tree_mask
+    bits = pack_tree_mask(torch.ones(1, 1, dtype=torch.int8, device="cuda"))[0]
+    out = []
+    tok = root
+    for i in range(n):
+        ids = torch.tensor([tok], device="cuda")
+        pos = torch.tensor([start + i], device="cuda")
+        hidden, _ = m.verify(ids, pos, bits, start + i)
+        tok = int(torch.argmax((hidden @ m.lm_head.t()).float(), dim=-1).item())
+        out.append(tok)
+    return out
+
+
+def test_greedy_speculative_decode_equals_target_greedy():
+    m = _model()
+    root = m.fill_context(PROMPT, seed=4)
+    want = _plain_greedy(m, root, PROMPT, 24)
+    r = m.diffspec_generate(PROMPT, max_new_tokens=24, nodes=8, max_depth=4, temperature=0.0, seed=4)
+    assert r["tokens"] == want
+    assert r["final_length"] == PROMPT + sum(a + 1 for a in r["accepted_per_step"])
+
+
+def test_chain_of_the_true_continuation_is_fully_accepted_and_compacted():
+    from specverify.runtime.draft_tree import finalize_tree
+    m = _model()
+    root = m.fill_context(PROMPT, seed=5)
+    want = _plain_greedy(m, root, PROMPT, 12)
+    depth = 5
+    # a width-1 tree: root -> want[0] -> ... -> want[depth-1]
+    tree = finalize_tree(torch.arange(depth, device="cuda"), torch.zeros(depth, 1, dtype=torch.int64, device="cuda"),
+                         torch.tensor(want[:depth], device="cuda").view(depth, 1), depth, 1, validate=True)
+    root_t = torch.tensor([root], device="cuda")
+    feat = torch.zeros(1, 3 * m.shape.hidden, device="cuda", dtype=m.dtype)
+    m.fill_context(PROMPT, seed=5)                      # the plain decode wrote past the prompt: restore
+    acc, _, _ = m.step(root_t, feat, PROMPT, 1, depth, 0.0, 0, 0, tree=tree)
+    h = acc.to_host()
+    assert h["accept_length"] == depth
+    assert h["best_candidate"][1:] == want[:depth]
+    assert h["next_token"] == want[depth]
+    # the compacted cache continues the same greedy sequence
+    rest = _plain_greedy(m, want[depth], PROMPT + depth + 1, 12 - depth - 1)
+    assert rest == want[depth + 1:12]
