@@ -188,8 +188,19 @@ size_t partial_bytes(const tv_attn_args* a, int splits) {
   return ((o + 255) & ~size_t(255)) + l;
 }
 
+// The tcgen05 kernel merges its own splits (fused combine) unless kernel bit
+// 8 (256) asks for the separate combine kernel.
+bool fused_combine(const tv_attn_args* a, const Plan& pl) { return pl.tc && pl.splits > 1 && !(a->kernel & 256); }
+
+// One int per (batch x KV head, row block): the fused combine's counters.
+size_t counter_bytes(const tv_attn_args* a, const Plan& pl) {
+  const int G = a->heads / a->kv_heads;
+  return (size_t)a->batch * a->kv_heads * tc_row_blocks(a->rows * G) * sizeof(int);
+}
+
 size_t workspace_for(const tv_attn_args* a, const Plan& pl) {
-  return pl.splits <= 1 ? 0 : partial_bytes(a, pl.splits);
+  if (pl.splits <= 1) return 0;
+  return ((partial_bytes(a, pl.splits) + 255) & ~size_t(255)) + (fused_combine(a, pl) ? counter_bytes(a, pl) : 0);
 }
 
 // Kernel parameters of a validated request; partials (when `partials`) in
@@ -313,9 +324,18 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
   AttnParams p;
   fill_params(a, pl, pl.splits > 1, p);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool fused = fused_combine(a, pl);
+  if (fused) {
+    // counters start at zero every call (a completed launch leaves them at
+    // zero too); the workspace may come from any allocator
+    const size_t off = (partial_bytes(a, pl.splits) + 255) & ~size_t(255);
+    p.counters = reinterpret_cast<int*>(static_cast<char*>(a->workspace) + off);
+    const cudaError_t e = cudaMemsetAsync(p.counters, 0, counter_bytes(a, pl), st);
+    if (e != cudaSuccess) return record_cuda_error(e);
+  }
   int rc = launch_attention(a, pl, p, st);
   if (rc != TV_OK) return rc;
-  if (pl.splits > 1) rc = launch_split_combine(p, a->dtype, a->head_dim, st);
+  if (pl.splits > 1 && !fused) rc = launch_split_combine(p, a->dtype, a->head_dim, st);
   return rc;
 }
 

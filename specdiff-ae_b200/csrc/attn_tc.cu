@@ -99,6 +99,7 @@ struct Bars {
   uint64_t ref_bar[4];      // per quarter: one phase per tile, the reference max is published
   uint32_t tmem;
   int abort;
+  int last;                 // fused combine: this CTA is its group's last split
   float mref[ROWS];         // reference max (log2 units) after the latest decided tile
   float xm[2 * ROWS];       // final references and partial sums of the two warps of a row
   float xl[2 * ROWS];
@@ -688,6 +689,36 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (valid && ch == 0) {
       if (prow) *part_lse_row(p, split, bh, r) = lse;
       else store_row_stats<T>(p, b, mm, hh, lse);
+    }
+    if (p.counters) {
+      // ---- fused split combine --------------------------------------------------
+      // Every split CTA of this (batch x KV head, row block) has written its
+      // partial; the last one to count itself in merges them all (the same
+      // log-sum-exp as split_combine_kernel), leaving the counter at zero.
+      __threadfence();
+      asm volatile("bar.sync 1, 256;" ::: "memory");   // the 8 softmax warps' partials are out
+      if (warp == 2 && lane == 0) {
+        int* ctr = p.counters + (int64_t)bh * gridDim.x + rb;
+        const int last = atomicAdd(ctr, 1) == (int)gridDim.z - 1;
+        if (last) *ctr = 0;
+        bars->last = last;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (bars->last) {
+        __threadfence();
+        for (int rr2 = warp - 2; rr2 < ROWS; rr2 += 8) {
+          const int r2 = rb * ROWS + rr2;
+          if (r2 >= p.R) break;
+          float4 o;
+          float l2;
+          combine_split_row<HD>(p, bh, r2, lane, o, l2);
+          int m2, h2;
+          row_coords(p, hk, r2, m2, h2);
+          store_out_pair<T>(p, b, m2, h2, 4 * lane, o.x, o.y);
+          store_out_pair<T>(p, b, m2, h2, 4 * lane + 2, o.z, o.w);
+          if (lane == 0) store_row_stats<T>(p, b, m2, h2, l2);
+        }
+      }
     }
   }
 
