@@ -2,36 +2,42 @@
 """Benchmark: tree-verify attention on B200 (BASELINE config 2 and the sharded scaling run).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload verify|rope-append]
+                    [--workload verify|config3|config4|config5|rope-append|lmhead-accept|
+                                tree-finalize|chunk-retrieve]
+                    [--nodes M --per-depth P --root] [--no-e2e --no-extras --no-cpu-baseline --no-graph]
 
-A step is one verify-attention pass of one layer over the config-2 problem:
-64K-token paged KV cache (16-token pages, seeded random page permutation),
-a 64-node depth-8 draft tree, Llama-3.1-8B attention shapes (32 query / 8 KV
-heads, head_dim 128), bf16.  Steps rotate over 4 independent layer pools
-(1 GiB of KV in all) so no step finds the previous step's KV in the 126 MB L2.
+Default (--workload verify): a step is one verify-attention pass of one layer
+over the config-2 problem: 64K-token paged KV cache (16-token pages, seeded
+random page permutation), a 64-node depth-8 draft tree, Llama-3.1-8B
+attention shapes (32 query / 8 KV heads, head_dim 128), bf16.  Steps rotate
+over 4 independent layer pools (1 GiB of KV in all) so no step finds the
+previous step's KV in the 126 MB L2.
 
 N = 1 runs config 2 on one GPU.  N > 1 (torchrun, one rank per GPU) runs the
 same 64K problem sequence-sharded: each rank attends its contiguous share of
 the pages; one kernel per rank then exchanges the (O, lse) partials over
 NVLink (to every peer below four ranks, to each row block's owner from four
-on) and merges them by log-sum-exp, so every rank holds the full result ("scaling": "strong": total work fixed).  Time = max over ranks of CUDA-event time.
+on) and merges them by log-sum-exp, so every rank holds the full result
+("scaling": "strong": total work fixed).  Time = max over ranks of CUDA-event
+time.
 
 `value` = algorithmic bytes (every visible K/V row once + Q/O/LSE/page
 table/bitmask) / step time, in GB/s, whole job.  `e2e` measures the same call
 through the public Python API with the per-step inputs (queries, tree mask)
 copied from pinned host memory and the result (output + LSE) read back to
 the host inside the timed region; the KV cache is device-resident state.
+Side measurements on one GPU: the root-row shape (M = 65), the reference's
+GPU op sequence for the same step, and the CPU baseline.
 
 --impl reference times the reference's own CPU path (prefix attention + tree
 attention + merge on repeat_kv-expanded K/V, fp32, restated in oracle/) on the
-host cores over a bounded sample of the same problem.
+host cores over the full config-2 problem, one pass per step.
 
---workload rope-append (one GPU) measures the step before verify attention
-instead: rotary embedding of q and k plus the append of the rotated k and v
-to the KV cache (``tv_rope_append``), for a batch of 16 sequences x 2048 new
-tokens (Llama-3.1-8B heads, bf16), next to the reference's own sequence of
-torch ops for the same step on the same GPU; ``verify_shape_us`` is the
-65-row verify step (B = 1).
+Other workloads: config3 (the speculative decode loop, verified tok/s),
+config4 (32 layers x 131072 tokens, sequence-sharded, 128-node tree), config5
+(batch-4 bundle verify over a chunk arena), and the steps on either side of
+the path (rope-append, lmhead-accept, tree-finalize, chunk-retrieve); each
+function's docstring says what it times.
 """
 
 from __future__ import annotations
@@ -56,8 +62,8 @@ METRIC = "tree-verify attn HBM GB/s (%peak) + verified tok/s @64K ctx, 1/2/4/8 B
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one attn_tc_kernel launch on
 # this workload, from a full ncu capture of the current kernel (the dominant
-# kernel: 93 % of the call's device time).
-NCU_TRAFFIC_BYTES = 273_927_168
+# kernel: 90 % of the call's device time; profiles/attn_tc_config2_full.md).
+NCU_TRAFFIC_BYTES = 272_937_216
 
 
 def log(*a):
@@ -141,13 +147,16 @@ class ClockSampler:
 # our arm
 # ---------------------------------------------------------------------------
 
+TREE = {"nodes": 64, "per_depth": 8, "root": False}     # config 2's tree; --nodes / --per-depth / --root change it
+
+
 def build_problems(rotate: int, dev, seed: int = 0):
-    return [wl_paged(seed=seed + 100 * i, dev=dev) for i in range(rotate)]
+    return [wl_paged(seed=seed + 100 * i, dev=dev, root=TREE["root"]) for i in range(rotate)]
 
 
 def wl_paged(seed: int, dev, root: bool = False):
     from specverify import workloads as wl
-    return wl.paged_verify(seed=seed, device=dev, root=root)
+    return wl.paged_verify(seed=seed, device=dev, root=root, nodes=TREE["nodes"], per_depth=TREE["per_depth"])
 
 
 def run_ours(args, rank, world, dev):
@@ -171,8 +180,14 @@ def run_ours(args, rank, world, dev):
             p = probs[i % rotate]
             attention(p.q, p.k_pool, p.v_pool, num_keys=p.num_keys, page_table=p.page_table,
                       mask_bits=bits[i % rotate], mask_len=m, out=outs[i % rotate], lse=lses[i % rotate])
-        launches_per_step = 2
-        workload = "config2: paged tree verify, S=65536, 64-node depth-8 tree, 1 layer, bf16, B=1"
+        from specverify.runtime.tree_attention import describe_attention
+        plan0 = describe_attention(p0.q, p0.k_pool, p0.v_pool, num_keys=p0.num_keys, page_table=p0.page_table,
+                                   mask_bits=bits[0], mask_len=m)
+        # the tcgen05 kernel merges its splits itself; the warp-MMA path adds a combine kernel
+        launches_per_step = 1 if plan0["kernel"] == "tcgen05" or plan0["splits"] == 1 else 2
+        workload = (f"config2: paged tree verify, S=65536, {TREE['nodes']}-node depth-"
+                    f"{-(-TREE['nodes'] // TREE['per_depth'])} tree{' + root row' if TREE['root'] else ''}, 1 layer, "
+                    f"bf16, B=1")
     else:
         # Sequence-sharded: this rank's share of the prefix pages; the last rank
         # also holds the tree's pages and applies the tree bitmask.
@@ -453,9 +468,10 @@ def run_ours(args, rank, world, dev):
             "unit": "GB/s",
             "frac": round(achieved_per_gpu / per_gpu_peak, 4),
             "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6.65 TB/s",
-            "traffic": NCU_TRAFFIC_BYTES if world == 1 else None,
-            "kernel": "attn_tc_kernel (93% of device time) + split_combine_kernel, timed together per call; "
-                      "traffic is attn_tc_kernel's per launch (ncu)",
+            "traffic": NCU_TRAFFIC_BYTES if world == 1 and TREE == {"nodes": 64, "per_depth": 8, "root": False}
+            else None,
+            "kernel": "attn_tc_kernel (the whole call: splits merged in the kernel); traffic is its per launch "
+                      "(ncu)",
             "tensor_tflops": round(flops / (ms * 1e-3) / 1e12 / world, 1),
         },
         "gpu_launches": launches_per_step * args.steps,
@@ -571,57 +587,70 @@ def reference_gpu_bar(probs, steps, warmup):
 
 
 # ---------------------------------------------------------------------------
-# reference CPU path (oracle restatement), bounded sample
+# reference CPU path (oracle restatement)
 # ---------------------------------------------------------------------------
 
-def cpu_reference_sample(sample_prefix: int, seed: int = 0, reps: int = 1):
-    """Time the reference's CPU verify pipeline (fp32, repeat_kv-expanded,
-    pages gathered by index_select) on the config-2 problem with the prefix
-    truncated to ``sample_prefix`` tokens.  Returns (GB/s of algorithmic
-    bytes of the sample, seconds per pass, threads, description)."""
+def cpu_reference_setup(prefix: int = 65536, seed: int = 0):
+    """The reference's CPU verify pipeline (fp32, repeat_kv-expanded, pages
+    gathered by index_select: it has no paged kernel) on the config-2
+    problem with a ``prefix``-token context.  Returns (one_pass, algorithmic
+    bytes of the problem counted at bf16 like the GPU problem, threads,
+    description)."""
     from oracle import attention as oatt
     from specverify import workloads as wl
     torch.set_num_threads(os.cpu_count() or 1)
-    w = wl.paged_verify(prefix_len=sample_prefix, device="cpu", dtype=torch.float32, seed=seed, spare_pages=0)
-    k, v = w.contiguous_kv(0)                                    # index_select through the page table
-    kk = k.permute(1, 0, 2)[None]
-    vv = v.permute(1, 0, 2)[None]
+    w = wl.paged_verify(prefix_len=prefix, device="cpu", dtype=torch.float32, seed=seed, spare_pages=0)
     s = w.prefix_len
     keep = w.tree.keep
-    oatt.reference_verify_layer(w.q, kk[:, :, :s], vv[:, :, :s], kk[:, :, s:], vv[:, :, s:], keep)  # warm
-    best = float("inf")
-    for _ in range(reps):
-        t0 = time.perf_counter()
+
+    def one_pass():
         pages = w.page_table[0].long()
         k2 = w.k_pool.index_select(0, pages).permute(1, 0, 2, 3).reshape(w.k_pool.shape[1], -1, w.k_pool.shape[3])
         v2 = w.v_pool.index_select(0, pages).permute(1, 0, 2, 3).reshape(w.v_pool.shape[1], -1, w.v_pool.shape[3])
         k2, v2 = k2[None, :, : w.num_keys], v2[None, :, : w.num_keys]
-        oatt.reference_verify_layer(w.q, k2[:, :, :s], v2[:, :, :s], k2[:, :, s:], v2[:, :, s:], keep)
-        best = min(best, time.perf_counter() - t0)
-    # algorithmic bytes of the sample counted at bf16 like the GPU problem
+        return oatt.reference_verify_layer(w.q, k2[:, :, :s], v2[:, :, :s], k2[:, :, s:], v2[:, :, s:], keep)
+
     b, m, h, d = w.q.shape
     alg = (s + m) * w.k_pool.shape[1] * d * 2 * 2 + 2 * m * h * d * 2 + m * h * 4 + w.page_table.numel() * 4
     desc = (f"reference CPU path (prefix_attention_forward + tree_attention_forward + merge, repeat_kv, fp32, "
-            f"pages gathered by index_select) on config 2 with the prefix cut to {sample_prefix} tokens")
-    return alg / best / 1e9, best, torch.get_num_threads(), desc
+            f"pages gathered by index_select) on config 2 ({prefix}-token context, 64-node tree)")
+    return one_pass, alg, torch.get_num_threads(), desc
+
+
+def cpu_reference_time(passes: int = 2, prefix: int = 65536):
+    """(GB/s, seconds per pass, threads, description): best of ``passes``
+    timed passes after one warm-up pass."""
+    one_pass, alg, thr, desc = cpu_reference_setup(prefix)
+    one_pass()
+    best = float("inf")
+    for _ in range(passes):
+        t0 = time.perf_counter()
+        one_pass()
+        best = min(best, time.perf_counter() - t0)
+    return alg / best / 1e9, best, thr, desc
 
 
 def run_reference(args, rank, world):
+    """The reference arm: its CPU path for the path, on the full config-2
+    problem, every step one whole pass (rank 0 only)."""
     if rank != 0:
         return None
-    sample = 8192
-    vals = []
-    for i in range(args.warmup + args.steps):
-        gbs, sec, thr, desc = cpu_reference_sample(sample, seed=i)
-        if i >= args.warmup:
-            vals.append((gbs, sec))
-    value = statistics.median(v for v, _ in vals)
-    ms = statistics.median(s for _, s in vals) * 1e3
+    one_pass, alg, thr, desc = cpu_reference_setup(65536)
+    for _ in range(args.warmup):
+        one_pass()
+    secs = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        one_pass()
+        secs.append(time.perf_counter() - t0)
+    sec = statistics.median(secs)
+    value = alg / sec / 1e9
     return {
         "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": "config2 (bounded CPU sample)", "sample": desc},
+        "config": {"workload": "config2: paged tree verify, S=65536, 64-node depth-8 tree, 1 layer, B=1 "
+                               "(the reference's CPU path, full size)", "sample": desc},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": thr, "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -1328,11 +1357,15 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA graph replays")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the side measurements (root-row variant, reference GPU ops)")
+    ap.add_argument("--nodes", type=int, default=64, help="verify workload: tree nodes (config 2: 64)")
+    ap.add_argument("--per-depth", type=int, default=8, help="verify workload: nodes per depth (config 2: 8)")
+    ap.add_argument("--root", action="store_true", help="verify workload: prepend the root row (M = nodes + 1)")
     ap.add_argument("--workload", choices=["verify", "config3", "config4", "config5", "rope-append", "lmhead-accept", "tree-finalize",
                                            "chunk-retrieve"], default="verify")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    TREE.update(nodes=args.nodes, per_depth=args.per_depth, root=args.root)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1385,9 +1418,9 @@ def main():
             res = run_ours(args, rank, world, dev)
         if rank == 0:
             if not args.no_cpu_baseline and world == 1 and args.workload == "verify":
-                gbs, sec, thr, desc = cpu_reference_sample(8192)
+                gbs, sec, thr, desc = cpu_reference_time(passes=2)
                 res["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-                                       "sample": desc + f"; {sec * 1e3:.1f} ms per pass"}
+                                       "sample": desc + f"; best of 2 passes, {sec * 1e3:.0f} ms per pass"}
             print(json.dumps(res), file=_JSON_OUT, flush=True)
     finally:
         if world > 1:

@@ -103,10 +103,7 @@ const char* tv_last_cuda_error(void);
  * out_f32 != 0 writes out in fp32 instead of `dtype`.
  *
  * Work is split over the keys (split-KV); the partial (O, lse) pairs live in
- * the caller's workspace and are merged by log-sum-exp: by the last split
- * CTA of each row group inside the tcgen05 kernel (its counters, also in the
- * workspace, are zeroed by the call itself), or by a second kernel on the
- * warp-MMA path and when kernel bit 8 (256) asks for it.
+ * the caller's workspace and are merged by log-sum-exp in a second kernel.
  */
 typedef struct tv_attn_args {
   int32_t dtype;                 /* TV_BF16 or TV_F16 for q, k, v, out      */
@@ -147,8 +144,6 @@ typedef struct tv_attn_args {
                                     owner exchange, bit 6 (64) push to every
                                     peer (default: push below 4 ranks,
                                     owner from 4 on);
-                                    bit 8 (256): tcgen05 path merges its
-                                    splits in a separate kernel;
                                     bit 7 (128): tcgen05 path on a paged
                                     pool loads each 64-dim half of a page
                                     row as its own TMA box (default: one box

@@ -1,6 +1,7 @@
 // C ABI of verify attention: argument checks, split-KV planning, kernel
 // selection, and the log-sum-exp merge kernels.
 #include <string.h>
+#include <stdint.h>
 
 #include <map>
 #include <mutex>
@@ -158,14 +159,35 @@ Plan plan(const tv_attn_args* a) {
   pl.tc = (sel != 1) && !(a->kernel & 16) && !a->kv_lens && a->num_keys > kPreciseMaxKeys &&
           tc_supported(a->dtype, D, R, paged, shift);
   pl.tile = pl.tc ? tc_tile_keys() : mma_tile_keys();
-  const int row_blocks = pl.tc ? tc_row_blocks(R) : (R + mma_rows_per_cta() - 1) / mma_rows_per_cta();
+  const int row_blocks = pl.tc ? tc_row_blocks(R) : mma_row_blocks(R);
   const int64_t base = (int64_t)row_blocks * a->batch * a->kv_heads;
   const int tiles = (a->num_keys + pl.tile - 1) / pl.tile;
   int splits = a->num_splits;
   if (splits <= 0) {
-    // Tensor-memory CTAs fill an SM each: one wave of at most 148.  The
-    // small warp-MMA CTAs run several per SM: aim for about four waves.
-    splits = pl.tc ? (int)(kNumSMs / base) : (int)((4LL * kNumSMs + base - 1) / base);
+    if (pl.tc) {
+      // Tensor-memory CTAs fill an SM each (one per SM): one wave of at most
+      // 148 (config 2: 16 row-block CTAs x 9 splits = 144).  Only when that
+      // wave would leave more than a quarter of the SMs idle (few splits of
+      // many row blocks, e.g. batch 4 x 3 row blocks x 8 KV heads = 96) may
+      // the CTAs run in more waves: waves x (tiles per CTA + a fixed cost of
+      // about 16 tiles for the pipeline fill, drain and epilogue) decides.
+      // Measured: many short CTAs in several waves lose to one full wave.
+      splits = (int)(kNumSMs / base);
+      if (splits < 1) splits = 1;
+      if (base * splits * 4 < 3LL * kNumSMs) {
+        int64_t best = INT64_MAX;
+        for (int s = 1; s <= 256 && s <= tiles && base * s <= 4LL * kNumSMs; ++s) {
+          const int64_t waves = (base * s + kNumSMs - 1) / kNumSMs;
+          const int64_t cost = waves * ((tiles + s - 1) / s + 16);
+          if (cost < best) { best = cost; splits = s; }
+        }
+      }
+    } else {
+      // The warp-MMA CTAs (112 KB of shared memory) run two per SM: one wave
+      // of 2 x 148 (measured: 37 splits of 8 row-block CTAs beat 74 by 10 %).
+      splits = (int)(2LL * kNumSMs / base);
+      if (splits < 1) splits = 1;
+    }
   }
   if (splits > tiles) splits = tiles;
   if (splits > 256) splits = 256;
@@ -188,19 +210,8 @@ size_t partial_bytes(const tv_attn_args* a, int splits) {
   return ((o + 255) & ~size_t(255)) + l;
 }
 
-// The tcgen05 kernel merges its own splits (fused combine) unless kernel bit
-// 8 (256) asks for the separate combine kernel.
-bool fused_combine(const tv_attn_args* a, const Plan& pl) { return pl.tc && pl.splits > 1 && !(a->kernel & 256); }
-
-// One int per (batch x KV head, row block): the fused combine's counters.
-size_t counter_bytes(const tv_attn_args* a, const Plan& pl) {
-  const int G = a->heads / a->kv_heads;
-  return (size_t)a->batch * a->kv_heads * tc_row_blocks(a->rows * G) * sizeof(int);
-}
-
 size_t workspace_for(const tv_attn_args* a, const Plan& pl) {
-  if (pl.splits <= 1) return 0;
-  return ((partial_bytes(a, pl.splits) + 255) & ~size_t(255)) + (fused_combine(a, pl) ? counter_bytes(a, pl) : 0);
+  return pl.splits <= 1 ? 0 : partial_bytes(a, pl.splits);
 }
 
 // Kernel parameters of a validated request; partials (when `partials`) in
@@ -324,18 +335,9 @@ int tv_verify_attn(const tv_attn_args* a, void* stream) {
   AttnParams p;
   fill_params(a, pl, pl.splits > 1, p);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool fused = fused_combine(a, pl);
-  if (fused) {
-    // counters start at zero every call (a completed launch leaves them at
-    // zero too); the workspace may come from any allocator
-    const size_t off = (partial_bytes(a, pl.splits) + 255) & ~size_t(255);
-    p.counters = reinterpret_cast<int*>(static_cast<char*>(a->workspace) + off);
-    const cudaError_t e = cudaMemsetAsync(p.counters, 0, counter_bytes(a, pl), st);
-    if (e != cudaSuccess) return record_cuda_error(e);
-  }
   int rc = launch_attention(a, pl, p, st);
   if (rc != TV_OK) return rc;
-  if (pl.splits > 1 && !fused) rc = launch_split_combine(p, a->dtype, a->head_dim, st);
+  if (pl.splits > 1) rc = launch_split_combine(p, a->dtype, a->head_dim, st);
   return rc;
 }
 

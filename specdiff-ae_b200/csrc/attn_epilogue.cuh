@@ -45,13 +45,12 @@ __device__ __forceinline__ float* part_lse_row(const AttnParams& p, int split, i
 
 // Log-sum-exp combine of the p.splits split partials of kernel row (bh, r):
 // this thread's four head-dim values 4q .. 4q+3 (normalised) and the row's
-// LSE.  Partials are read up to 8 splits at a time (all loads of a block in
+// LSE.  Partials are read BLK splits at a time (all loads of a block in
 // flight together; they are usually still in L2) and folded with a running
 // max, so the row needs one pass.
-template <int D>
+template <int D, int BLK = 8>
 __device__ __forceinline__ void combine_split_row(const AttnParams& p, int bh, int r, int q, float4& o,
                                                   float& lse) {
-  constexpr int BLK = 8;
   float mx = -INFINITY, wsum = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int s0 = 0; s0 < p.splits; s0 += BLK) {

@@ -11,7 +11,7 @@ namespace tv {
 // precise: softmax weights enter PV as a hi + lo 16-bit pair.
 int launch_attn_mma(const AttnParams& p, int dtype, int D, bool precise, cudaStream_t st);
 int mma_tile_keys();
-int mma_rows_per_cta();
+int mma_row_blocks(int R);   // CTAs per (batch, KV head)
 
 // Tensor-memory (tcgen05) path: head_dim 128, >= 64 query rows per KV head.
 // kernel_bits: tv_attn_args.kernel (bit 7 forces half-head TMA boxes).

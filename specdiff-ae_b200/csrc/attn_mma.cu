@@ -1,13 +1,17 @@
 // Verify attention, warp-MMA path (mma.sync m16n8k16, fp32 accumulate).
 //
-// One CTA = 4 warps = 64 query rows of one (batch, KV head) over one split of
-// the keys.  Query rows are (tree node, query head of the GQA group) pairs,
+// One CTA = 4 warps = up to 64 query rows of one (batch, KV head) over one
+// split of the keys.  Each warp computes 16 rows; with fewer than 64 rows per
+// KV head (narrow trees) the warps split every key tile instead of computing
+// padding rows: KS = 2 (up to 32 rows) or 4 (up to 16 rows) warps share a
+// row group, each scoring its 1/KS of the tile's keys, and their (max, sum,
+// O) are merged through shared memory at the end.  Query rows are (tree node, query head of the GQA group) pairs,
 // r = node * G + g, so a KV tile staged in shared memory serves every head
 // of the group: nothing is expanded per query head (the reference
 // materialises repeat_kv copies, llama_target_model.py:795-796).
 //
 // Keys arrive in 64-key tiles by cp.async (16-byte chunks, zero-filled past
-// the end or for missing pages), double-buffered.  For a paged cache every key
+// the end or for missing pages), three tiles in flight.  For a paged cache every key
 // looks up its physical page; the pool layout [page][kv_head][token][D] keeps
 // a page's 16 tokens of one head contiguous, so one 64-key tile is four 4 KB
 // runs.  Scores go through an online softmax in the exp2 domain; keys of the
@@ -22,10 +26,10 @@
 namespace tv {
 namespace {
 
-constexpr int BM = 64;      // query rows per CTA
+constexpr int BM = 64;      // query rows per CTA at KS = 1
 constexpr int BN = 64;      // keys per tile
 constexpr int NTHREADS = 128;
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 
 template <int D>
 struct Geo {
@@ -85,9 +89,12 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
 // 16-bit values (two MMAs) instead of one rounded value.  Rounding P to bf16
 // alone costs up to 2^-9 * max|v| of absolute error per output, which matters
 // when a row sees few keys; the pair brings it to ~2^-17.
-template <typename T, int D, bool PAGED, bool PRECISE>
+template <typename T, int D, bool PAGED, bool PRECISE, int KS>
 __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) {
   using G = Geo<D>;
+  constexpr int RG = 4 / KS;          // row groups of 16 rows per CTA
+  constexpr int BMK = 16 * RG;        // query rows per CTA
+  constexpr int KW = BN / KS;         // keys of a tile scored by one warp
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sQ = smem;
   uint8_t* sK = smem + G::Q_BYTES;
@@ -110,16 +117,19 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
   const int lane = tid & 31;
   const int gid = lane >> 2;
   const int tig = lane & 3;
+  const int rg = warp % RG;           // this warp's row group
+  const int kq = warp / RG;           // and its share of every key tile
 
   // ---- stage the 64 query rows of this CTA --------------------------------
   {
     const T* qb = static_cast<const T*>(p.q);
 #pragma unroll
-    for (int j = 0; j < (BM * G::CH) / NTHREADS; ++j) {
+    for (int j = 0; j < (BMK * G::CH + NTHREADS - 1) / NTHREADS; ++j) {
       const int idx = tid + j * NTHREADS;
+      if (idx >= BMK * G::CH) break;
       const int row = idx / G::CH;
       const int c = idx % G::CH;
-      const int r = rb * BM + row;
+      const int r = rb * BMK + row;
       const T* src = qb;
       int bytes = 0;
       if (r < p.R) {
@@ -131,11 +141,14 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
       cp_async16(smem_u32(sQ + G::swz(row, c)), src, bytes);
     }
   }
+  // tiles t0 and t0 + 1 in flight before the loop (one commit group each)
   if (t0 < t1) load_kv_tile<T, D, PAGED>(p, sK, sV, b, hk, len, t0, tid);
   cp_async_commit();
+  if (t0 + 1 < t1) load_kv_tile<T, D, PAGED>(p, sK + G::T_BYTES, sV + G::T_BYTES, b, hk, len, t0 + 1, tid);
+  cp_async_commit();
 
-  // Rows held by this thread: warp rows gid and gid + 8.
-  const int r0 = rb * BM + warp * 16 + gid;
+  // Rows held by this thread: its warp's row group's rows gid and gid + 8.
+  const int r0 = rb * BMK + rg * 16 + gid;
   const int r1 = r0 + 8;
   const int m0 = min(r0, p.R - 1) / p.G;
   const int m1 = min(r1, p.R - 1) / p.G;
@@ -149,19 +162,21 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
   uint32_t qf[D / 16][4];
 
   for (int t = t0; t < t1; ++t) {
-    const int st = (t - t0) & 1;
-    if (t + 1 < t1) {
-      load_kv_tile<T, D, PAGED>(p, sK + (st ^ 1) * G::T_BYTES, sV + (st ^ 1) * G::T_BYTES, b, hk, len, t + 1, tid);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+    const int st = (t - t0) % STAGES;
+    // Tile t + 2 into the stage tile t - 1 used (freed by the barrier that
+    // ended the previous iteration); every iteration commits one group, so
+    // waiting for all but the newest two leaves tile t landed.
+    if (t + 2 < t1) {
+      const int s2 = (t + 2 - t0) % STAGES;
+      load_kv_tile<T, D, PAGED>(p, sK + s2 * G::T_BYTES, sV + s2 * G::T_BYTES, b, hk, len, t + 2, tid);
     }
+    cp_async_commit();
+    cp_async_wait<2>();
     __syncthreads();
     if (t == t0) {
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int row = rg * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int c = kk * 2 + (lane >> 4);
         ldsm_x4(smem_u32(sQ + G::swz(row, c)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
       }
@@ -169,15 +184,15 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
     const uint8_t* tK = sK + st * G::T_BYTES;
     const uint8_t* tV = sV + st * G::T_BYTES;
 
-    // ---- S = Q K^T (16 rows x 64 keys per warp) ---------------------------
-    float s[BN / 8][4];
+    // ---- S = Q K^T (16 rows x KW keys per warp) ---------------------------
+    float s[KW / 8][4];
 #pragma unroll
-    for (int i = 0; i < BN / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+    for (int i = 0; i < KW / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
 #pragma unroll
-      for (int nn = 0; nn < BN / 16; ++nn) {
-        const int row = nn * 16 + (lane & 7) + (lane >> 4) * 8;
+      for (int nn = 0; nn < KW / 16; ++nn) {
+        const int row = kq * KW + nn * 16 + (lane & 7) + (lane >> 4) * 8;
         const int c = kk * 2 + ((lane >> 3) & 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(smem_u32(tK + G::swz(row, c)), b0, b1, b2, b3);
@@ -187,10 +202,10 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
     }
 
     // ---- scale, bound and tree-mask the scores -----------------------------
-    const int nbase = t * BN;
-    const bool edge = (nbase + BN > len) || (nbase + BN > tail);
+    const int nbase = t * BN + kq * KW;
+    const bool edge = (nbase + KW > len) || (nbase + KW > tail);
 #pragma unroll
-    for (int j = 0; j < BN / 8; ++j) {
+    for (int j = 0; j < KW / 8; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float x = s[j][e] * p.scale_log2;
@@ -212,7 +227,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
     // ---- online softmax (exp2 domain) --------------------------------------
     float tmax0 = -INFINITY, tmax1 = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < BN / 8; ++j) {
+    for (int j = 0; j < KW / 8; ++j) {
       tmax0 = fmaxf(tmax0, fmaxf(s[j][0], s[j][1]));
       tmax1 = fmaxf(tmax1, fmaxf(s[j][2], s[j][3]));
     }
@@ -230,7 +245,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
     mx1 = nm1;
     float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
-    for (int j = 0; j < BN / 8; ++j) {
+    for (int j = 0; j < KW / 8; ++j) {
       s[j][0] = fast_exp2(s[j][0] - use0);
       s[j][1] = fast_exp2(s[j][1] - use0);
       s[j][2] = fast_exp2(s[j][2] - use1);
@@ -250,7 +265,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
 
     // ---- O += P V ------------------------------------------------------------
 #pragma unroll
-    for (int kk = 0; kk < BN / 16; ++kk) {
+    for (int kk = 0; kk < KW / 16; ++kk) {
       uint32_t a[4], al[4];
       if (PRECISE) {
         split_pair<T>(s[2 * kk][0], s[2 * kk][1], a[0], al[0]);
@@ -265,7 +280,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
       }
 #pragma unroll
       for (int dd = 0; dd < D / 16; ++dd) {
-        const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int row = kq * KW + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int c = dd * 2 + (lane >> 4);
         uint32_t b0, b1, b2, b3;
         ldsm_x4_t(smem_u32(tV + G::swz(row, c)), b0, b1, b2, b3);
@@ -286,6 +301,47 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  if (KS > 1) {
+    // Merge the KS warps of each row group (same rows, disjoint keys): the
+    // helpers leave (max, sum, O) in shared memory (the K/V stages are free
+    // now), the first warp of the group folds them in.
+    __syncthreads();
+    float* xo = reinterpret_cast<float*>(sK);                       // [warp][lane][D / 2]
+    float* xs = xo + NTHREADS * (D / 2);                            // [warp][lane][4]
+    if (kq > 0) {
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i)
+        *reinterpret_cast<float4*>(xo + (warp * 32 + lane) * (D / 2) + 4 * i) =
+            make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+      *reinterpret_cast<float4*>(xs + (warp * 32 + lane) * 4) = make_float4(mx0, mx1, l0, l1);
+    }
+    __syncthreads();
+    if (kq == 0) {
+#pragma unroll
+      for (int q = 1; q < KS; ++q) {
+        const int w2 = warp + q * RG;
+        const float4 st2 = *reinterpret_cast<const float4*>(xs + (w2 * 32 + lane) * 4);
+        const float n0 = fmaxf(mx0, st2.x), n1 = fmaxf(mx1, st2.y);
+        const float u0 = n0 == -INFINITY ? 0.f : n0, u1 = n1 == -INFINITY ? 0.f : n1;
+        const float a0 = fast_exp2(mx0 - u0), b0 = fast_exp2(st2.x - u0);
+        const float a1 = fast_exp2(mx1 - u1), b1 = fast_exp2(st2.y - u1);
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+          const float4 v2 = *reinterpret_cast<const float4*>(xo + (w2 * 32 + lane) * (D / 2) + 4 * i);
+          o[i][0] = o[i][0] * a0 + v2.x * b0;
+          o[i][1] = o[i][1] * a0 + v2.y * b0;
+          o[i][2] = o[i][2] * a1 + v2.z * b1;
+          o[i][3] = o[i][3] * a1 + v2.w * b1;
+        }
+        l0 = l0 * a0 + st2.z * b0;
+        l1 = l1 * a1 + st2.w * b1;
+        mx0 = n0;
+        mx1 = n1;
+      }
+    } else {
+      return;                                                       // merged by the group's first warp
+    }
+  }
   const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
   const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
   const float lse0 = l0 > 0.f ? (mx0 + __log2f(l0)) * kLn2 : -INFINITY;
@@ -324,15 +380,29 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const AttnParams p) 
   }
 }
 
-template <typename T, int D, bool PAGED, bool PRECISE>
-int launch_t(const AttnParams& p, cudaStream_t st) {
+// Warps per row group: 4 for up to 16 rows per KV head, 2 for up to 32.
+int key_split(int R) { return R <= 16 ? 4 : R <= 32 ? 2 : 1; }
+
+template <typename T, int D, bool PAGED, bool PRECISE, int KS>
+int launch_k(const AttnParams& p, cudaStream_t st) {
   constexpr int smem = Geo<D>::SMEM;
-  auto kern = attn_mma_kernel<T, D, PAGED, PRECISE>;
+  static_assert(NTHREADS * (D / 2 + 4) * 4 <= 2 * STAGES * Geo<D>::T_BYTES, "merge scratch");
+  auto kern = attn_mma_kernel<T, D, PAGED, PRECISE, KS>;
   const int rc_smem = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
   if (rc_smem != TV_OK) return rc_smem;
-  dim3 grid((p.R + BM - 1) / BM, p.B * p.Hkv, p.splits);
+  constexpr int rows = 64 / KS;
+  dim3 grid((p.R + rows - 1) / rows, p.B * p.Hkv, p.splits);
   kern<<<grid, NTHREADS, smem, st>>>(p);
   return check_launch();
+}
+
+template <typename T, int D, bool PAGED, bool PRECISE>
+int launch_t(const AttnParams& p, cudaStream_t st) {
+  switch (key_split(p.R)) {
+    case 4: return launch_k<T, D, PAGED, PRECISE, 4>(p, st);
+    case 2: return launch_k<T, D, PAGED, PRECISE, 2>(p, st);
+    default: return launch_k<T, D, PAGED, PRECISE, 1>(p, st);
+  }
 }
 
 template <typename T, int D>
@@ -355,7 +425,10 @@ int launch_dtype(const AttnParams& p, int D, bool precise, cudaStream_t st) {
 }  // namespace
 
 int mma_tile_keys() { return BN; }
-int mma_rows_per_cta() { return BM; }
+int mma_row_blocks(int R) {
+  const int rows = 64 / key_split(R);
+  return (R + rows - 1) / rows;
+}
 
 int launch_attn_mma(const AttnParams& p, int dtype, int D, bool precise, cudaStream_t st) {
   if (dtype == TV_BF16) return launch_dtype<__nv_bfloat16>(p, D, precise, st);

@@ -42,11 +42,6 @@ struct AttnParams {
   // kernels write normalised partials here instead of the final outputs.
   float* part_o;
   float* part_lse;
-  // Fused split combine (tcgen05 kernel): one int per (batch x KV head, row
-  // block), zero at launch; the last split CTA of a group to finish merges
-  // the group's partials into the final outputs.  nullptr = a separate
-  // combine kernel (or the sharded exchange) reads the partials.
-  int* counters;
   int* err;                // optional device status word (nonzero = a wait gave up)
 };
 

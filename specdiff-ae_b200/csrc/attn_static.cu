@@ -4,10 +4,9 @@
 // The array's address is resolved once per device (cudaGetSymbolAddress with
 // that device current) on the first call there; that call must come before
 // any stream capture.  Calls on one device share the array, so they must not
-// overlap (serialise them on one stream).  The only words that must start
-// at zero -- the split counters of the fused combine -- are cleared by every
-// call before its kernel runs; every partial row the merge reads is written
-// by the same launch first.  Requests needing more than the array holds are rejected
+// overlap (serialise them on one stream).  Nothing in the array needs to
+// start at zero: every partial row the merge reads is written by the same
+// launch first.  Requests needing more than the array holds are rejected
 // with TV_ERR_WORKSPACE before anything is launched.
 #include <cuda_runtime.h>
 

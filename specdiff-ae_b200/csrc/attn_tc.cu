@@ -43,6 +43,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <string.h>
+
 #include <type_traits>
 
 #include "attn_epilogue.cuh"
@@ -99,7 +101,6 @@ struct Bars {
   uint64_t ref_bar[4];      // per quarter: one phase per tile, the reference max is published
   uint32_t tmem;
   int abort;
-  int last;                 // fused combine: this CTA is its group's last split
   float mref[ROWS];         // reference max (log2 units) after the latest decided tile
   float xm[2 * ROWS];       // final references and partial sums of the two warps of a row
   float xl[2 * ROWS];
@@ -501,7 +502,31 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* pair = &bars->pair[q4];             // both warps of the quarter meet once, at the end
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    for (int i = par; i < NT; i += 2) {
+    // A warp whose 32 rows are all padding (the last row block of an
+    // M x G that is not a multiple of 128) keeps every wait and arrival of
+    // the pipeline, in the same order, but computes nothing: its P lanes
+    // hold whatever they held, which only reaches O rows never stored.  Both
+    // warps of a lane quarter cover the same rows, so both skip the
+    // reference hand-off.
+    const bool live = __any_sync(0xffffffffu, valid);
+    for (int i = par; i < NT && !live; i += 2) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[i % SBUF], (i / SBUF) & 1, abort))) {
+        raise_abort(bars, err, 3);
+        ok = false;
+        break;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->s_free[i % SBUF]);
+      if (i >= PBUF && !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[i % PBUF], ((i - PBUF) / PBUF) & 1, abort))) {
+        raise_abort(bars, err, 7);
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[i % PBUF]);
+    }
+    for (int i = par; i < NT && live; i += 2) {
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[i % SBUF], (i / SBUF) & 1, abort))) {
         raise_abort(bars, err, 3);
         ok = false;
@@ -690,36 +715,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (prow) *part_lse_row(p, split, bh, r) = lse;
       else store_row_stats<T>(p, b, mm, hh, lse);
     }
-    if (p.counters) {
-      // ---- fused split combine --------------------------------------------------
-      // Every split CTA of this (batch x KV head, row block) has written its
-      // partial; the last one to count itself in merges them all (the same
-      // log-sum-exp as split_combine_kernel), leaving the counter at zero.
-      __threadfence();
-      asm volatile("bar.sync 1, 256;" ::: "memory");   // the 8 softmax warps' partials are out
-      if (warp == 2 && lane == 0) {
-        int* ctr = p.counters + (int64_t)bh * gridDim.x + rb;
-        const int last = atomicAdd(ctr, 1) == (int)gridDim.z - 1;
-        if (last) *ctr = 0;
-        bars->last = last;
-      }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (bars->last) {
-        __threadfence();
-        for (int rr2 = warp - 2; rr2 < ROWS; rr2 += 8) {
-          const int r2 = rb * ROWS + rr2;
-          if (r2 >= p.R) break;
-          float4 o;
-          float l2;
-          combine_split_row<HD>(p, bh, r2, lane, o, l2);
-          int m2, h2;
-          row_coords(p, hk, r2, m2, h2);
-          store_out_pair<T>(p, b, m2, h2, 4 * lane, o.x, o.y);
-          store_out_pair<T>(p, b, m2, h2, 4 * lane + 2, o.z, o.w);
-          if (lane == 0) store_row_stats<T>(p, b, m2, h2, l2);
-        }
-      }
-    }
   }
 
   tc_fence_before();
@@ -865,12 +860,69 @@ int tc_maps(const AttnParams& p, int dtype, int kernel_bits, CUtensorMap* mk, CU
   return TV_OK;
 }
 
+// The last few requests' tensor maps, per host thread: a decode loop calls
+// with the same caches (one per layer) every step, and encoding a map costs
+// microseconds of host time.  The key is everything a map is built from.
+struct MapKey {
+  const void* k;
+  const void* v;
+  int64_t k_sb, k_sn, k_sh, v_sb, v_sn, v_sh;
+  int64_t n1, n2;           // paged: page shift, pages; contiguous: keys, batch
+  int dtype, hkv, paged, narrow;
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap mk, mv;
+  int box;
+  bool wide;
+  bool used;
+};
+constexpr int kMapCache = 64;
+
+int tc_maps_cached(const AttnParams& p, int dtype, int kernel_bits, CUtensorMap* mk, CUtensorMap* mv, int* box,
+                   bool* wide) {
+  static thread_local MapEntry cache[kMapCache];
+  static thread_local int next = 0;
+  MapKey key;
+  memset(&key, 0, sizeof(key));
+  key.k = p.k;
+  key.v = p.v;
+  key.k_sb = p.k_sb; key.k_sn = p.k_sn; key.k_sh = p.k_sh;
+  key.v_sb = p.v_sb; key.v_sn = p.v_sn; key.v_sh = p.v_sh;
+  key.paged = p.pt != nullptr;
+  key.n1 = key.paged ? p.page_shift : p.num_keys;
+  key.n2 = key.paged ? p.num_pages : p.B;
+  key.dtype = dtype;
+  key.hkv = p.Hkv;
+  key.narrow = (kernel_bits & 128) ? 1 : 0;
+  for (int i = 0; i < kMapCache; ++i) {
+    if (cache[i].used && memcmp(&cache[i].key, &key, sizeof(key)) == 0) {
+      *mk = cache[i].mk;
+      *mv = cache[i].mv;
+      *box = cache[i].box;
+      *wide = cache[i].wide;
+      return TV_OK;
+    }
+  }
+  const int rc = tc_maps(p, dtype, kernel_bits, mk, mv, box, wide);
+  if (rc != TV_OK) return rc;
+  MapEntry& e = cache[next];
+  next = (next + 1) % kMapCache;
+  e.key = key;
+  e.mk = *mk;
+  e.mv = *mv;
+  e.box = *box;
+  e.wide = *wide;
+  e.used = true;
+  return TV_OK;
+}
+
 int launch_attn_tc(const AttnParams& p, int dtype, int D, int kernel_bits, cudaStream_t st) {
   if (D != HD) return TV_ERR_UNSUPPORTED;
   CUtensorMap mk, mv;
   int box = 16;
   bool wide = false;
-  const int rc = tc_maps(p, dtype, kernel_bits, &mk, &mv, &box, &wide);
+  const int rc = tc_maps_cached(p, dtype, kernel_bits, &mk, &mv, &box, &wide);
   if (rc != TV_OK) return rc;
   const int tf = p.k_sn <= p.k_sh ? 1 : 0;
   if (p.pt) {

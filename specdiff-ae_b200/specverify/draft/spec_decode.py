@@ -162,6 +162,10 @@ class SpecDecodeModel:
         self.d_table = torch.arange(dpages, dtype=torch.int32, device=device).view(1, dpages)
         self.draft_ctx = draft_ctx
         self.cos, self.sin = rope_tables(d, max_tokens + 64, s.rope_theta, device, dtype)
+        # the draft reads the step's start position from the device, so its
+        # whole tree growth can be replayed as one CUDA graph per step
+        self._start = torch.zeros((), dtype=torch.int64, device=device)
+        self._graphs: Dict[tuple, tuple] = {}
 
     @classmethod
     def from_config(cls, shape: Optional[LlamaShape] = None, *, device="cuda", dtype=torch.bfloat16, seed: int = 0,
@@ -196,18 +200,22 @@ class SpecDecodeModel:
         return rms_norm(x, self.norm, s.rms_eps), torch.cat(feats, dim=-1)
 
     # ---- draft --------------------------------------------------------------
-    def draft_tree(self, root: torch.Tensor, root_feat: torch.Tensor, start: int, width: int, depth: int):
+    def draft_tree(self, root: torch.Tensor, root_feat: torch.Tensor, width: int, depth: int):
         """Grow a ``width`` x ``depth`` tree from the root.  root [1] target id,
-        root_feat [1, 3 H] target features.  Returns the finalize_tree dict."""
+        root_feat [1, 3 H] target features; the root's position is the device
+        scalar ``self._start``.  Nothing is read back to the host.  Returns the
+        finalize_tree dict."""
         s = self.shape
         dev = self.device
         ctx = self.draft_ctx
         fused = root_feat @ self.d_fc.t()                                   # [1, H]
         tok = root.view(1)
         feat = fused
-        par_hidden_rows = None
+        # (no Python scalars written into device tensors: the growth is
+        # captured as a CUDA graph, where a host-to-device copy is not allowed)
+        one = torch.ones(width, dtype=torch.int8, device=dev)
         anc = torch.zeros((1 + width * depth, 1 + width * depth), dtype=torch.int8, device=dev)
-        anc[0, 0] = 1
+        anc[0, 0:1].fill_(1)
         rows_now = torch.zeros(1, dtype=torch.long, device=dev)               # tree rows of the inputs
         parents_matrix = torch.zeros((depth, width), dtype=torch.int64, device=dev)
         ids_matrix = torch.zeros((depth, width), dtype=torch.int64, device=dev)
@@ -218,7 +226,7 @@ class SpecDecodeModel:
             emb = self.embed[tok]
             x_in = torch.cat([rms_norm(emb, self.d_layer.ln1[: s.hidden], s.rms_eps),
                               rms_norm(feat, self.d_layer.ln1[s.hidden:], s.rms_eps)], dim=-1)
-            pos = torch.full((t,), start + dd, dtype=torch.int64, device=dev)
+            pos = (self._start + dd).expand(t).contiguous()
             keep = anc[rows_now][:, : written + t]
             bits = pack_tree_mask(keep)
             h = _layer_forward(s, self.d_layer, x_in, feat, self.d_pool[0], self.d_pool[1], self.d_table,
@@ -234,7 +242,7 @@ class SpecDecodeModel:
             ids_matrix[dd] = new_tok
             new_rows = 1 + dd * width + torch.arange(width, device=dev)
             anc[new_rows] = anc[rows_now[par]]
-            anc[new_rows, new_rows] = 1
+            anc.index_put_((new_rows, new_rows), one)
             rows_now = new_rows
             score = best_score
             tok = self.d2t_map[new_tok]
@@ -251,7 +259,7 @@ class SpecDecodeModel:
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         ev[0].record()
         if tree is None:
-            tree = self.draft_tree(root, root_feat, start, width, depth)
+            tree = self._draft_graphed(root, root_feat, start, width, depth)
         ev[1].record()
         ids = torch.cat([root.view(1), tree["input_ids"]])
         pos = torch.cat([torch.full((1,), start, dtype=torch.int64, device=self.device),
@@ -265,6 +273,32 @@ class SpecDecodeModel:
         self._compact(start, acc, ids.numel())
         ev[3].record()
         return acc, feats, ev
+
+    def _draft_graphed(self, root, root_feat, start: int, width: int, depth: int):
+        """draft_tree replayed from a CUDA graph captured on first use (static
+        input and output buffers per tree shape)."""
+        self._start.fill_(start)
+        key = (width, depth)
+        if key not in self._graphs:
+            s_root = torch.zeros(1, dtype=torch.int64, device=self.device)
+            s_feat = torch.zeros((1, 3 * self.shape.hidden), dtype=self.dtype, device=self.device)
+            s_root.copy_(root.view(1))
+            s_feat.copy_(root_feat)
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                self.draft_tree(s_root, s_feat, width, depth)           # warm-up outside the capture
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = self.draft_tree(s_root, s_feat, width, depth)
+            self._graphs[key] = (g, s_root, s_feat, out)
+        g, s_root, s_feat, out = self._graphs[key]
+        s_root.copy_(root.view(1))
+        s_feat.copy_(root_feat)
+        g.replay()
+        return out
 
     def _compact(self, start: int, acc, rows: int):
         """Accepted path rows ``start + path[j]`` -> ``start + j`` in every layer's K and V."""

@@ -161,20 +161,64 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     the tcgen05 kernel skip masking key tiles every row fully sees.
     Returns ``out``.
     """
-    a, out = attn_args(q, k, v, num_keys=num_keys, kv_lens=kv_lens, page_table=page_table, mask_bits=mask_bits,
-                       mask_len=mask_len, out=out, out_f32=out_f32, lse=lse, lse_strides=lse_strides,
-                       aux_lse=aux_lse, aux_strides=aux_strides, weight=weight, weight_strides=weight_strides,
-                       scale=scale, num_splits=num_splits, kernel=kernel, status=status, mask_full=mask_full)
     lib = _lib.load()
-    need = ctypes.c_size_t(0)
-    _lib.check(lib.tv_attn_workspace_size(ctypes.byref(a), ctypes.byref(need)), "tv_attn_workspace_size")
+    # Fast path: a request whose shapes, strides, dtypes, devices and options
+    # were validated before reuses that call's argument block and workspace
+    # size; only the data pointers change.  A decode loop calls this once per
+    # layer with the same geometry every step.
+    key = _request_key(q, k, v, num_keys, kv_lens, page_table, mask_bits, mask_len, out, out_f32, lse,
+                       lse_strides, aux_lse, aux_strides, weight, weight_strides, scale, num_splits, kernel, status,
+                       mask_full)
+    hit = _PLANS.get(key)
+    if hit is None:
+        a, out = attn_args(q, k, v, num_keys=num_keys, kv_lens=kv_lens, page_table=page_table,
+                           mask_bits=mask_bits, mask_len=mask_len, out=out, out_f32=out_f32, lse=lse,
+                           lse_strides=lse_strides, aux_lse=aux_lse, aux_strides=aux_strides, weight=weight,
+                           weight_strides=weight_strides, scale=scale, num_splits=num_splits, kernel=kernel,
+                           status=status, mask_full=mask_full)
+        need = ctypes.c_size_t(0)
+        _lib.check(lib.tv_attn_workspace_size(ctypes.byref(a), ctypes.byref(need)), "tv_attn_workspace_size")
+        if len(_PLANS) >= 512:
+            _PLANS.clear()
+        _PLANS[key] = (bytes(a), need.value)
+        need = need.value
+    else:
+        a = _lib.AttnArgs.from_buffer_copy(hit[0])
+        need = hit[1]
+        if out is None:
+            b, m, h, d = q.shape
+            out = torch.empty((b, m, h, d), dtype=torch.float32 if out_f32 else q.dtype, device=q.device)
+        a.q, a.k, a.v, a.out = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+        a.page_table = page_table.data_ptr() if page_table is not None else None
+        a.kv_lens = kv_lens.data_ptr() if kv_lens is not None else None
+        a.mask = mask_bits.data_ptr() if mask_len else None
+        a.lse = lse.data_ptr() if lse is not None else None
+        a.aux_lse = aux_lse.data_ptr() if aux_lse is not None else None
+        a.weight = weight.data_ptr() if aux_lse is not None else None
+        a.status = status.data_ptr() if status is not None else None
+        a.mask_words_full = mask_full.data_ptr() if (mask_len and mask_full is not None) else None
     ws = None
-    if need.value:
-        ws = torch.empty(need.value, dtype=torch.uint8, device=out.device)
+    if need:
+        ws = torch.empty(need, dtype=torch.uint8, device=out.device)
         a.workspace = ws.data_ptr()
-        a.workspace_bytes = need.value
+        a.workspace_bytes = need
     _lib.check(lib.tv_verify_attn(ctypes.byref(a), _lib.stream_ptr(out.device)), "tv_verify_attn")
     return out
+
+
+_PLANS: dict = {}
+
+
+def _geom(t):
+    """Everything of a tensor argument but its data pointer (None stays None)."""
+    return None if t is None else (t.shape, t.stride(), t.dtype, t.device)
+
+
+def _request_key(q, k, v, num_keys, kv_lens, page_table, mask_bits, mask_len, out, out_f32, lse, lse_strides,
+                 aux_lse, aux_strides, weight, weight_strides, scale, num_splits, kernel, status, mask_full):
+    return (_geom(q), _geom(k), _geom(v), num_keys, _geom(kv_lens), _geom(page_table), _geom(mask_bits),
+            int(mask_len), _geom(out), bool(out_f32), _geom(lse), lse_strides, _geom(aux_lse), aux_strides,
+            _geom(weight), weight_strides, scale, int(num_splits), int(kernel), _geom(status), _geom(mask_full))
 
 
 def describe_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, **kw) -> dict:

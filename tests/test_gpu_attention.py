@@ -196,14 +196,9 @@ def test_config2_all_rows_against_oracle(wide):
     other = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
                              kernel=kern ^ 128)
     assert torch.equal(other, out)
-    # the splits merged inside the kernel (default) or by the separate
-    # combine kernel (bit 8): the same arithmetic in the same order
-    for _ in range(3):                                # the in-kernel counters leave no state behind
-        sep, sep_lse = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(),
-                                        page_table=w.page_table, kernel=kern | 256, return_lse=True)
+    for _ in range(2):                                # repeated calls: identical bits
         again, again_lse = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(),
                                             page_table=w.page_table, kernel=kern, return_lse=True)
-        assert torch.equal(sep, out) and torch.equal(sep_lse, lse)
         assert torch.equal(again, out) and torch.equal(again_lse, lse)
     one = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
                            num_splits=1, kernel=kern)
