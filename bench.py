@@ -63,7 +63,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one attn_tc_kernel launch on
 # this workload, from a full ncu capture of the current kernel (the dominant
 # kernel: 90 % of the call's device time; profiles/attn_tc_config2_full.md).
-NCU_TRAFFIC_BYTES = 272_937_216
+NCU_TRAFFIC_BYTES = 273_847_808
 
 
 def log(*a):
@@ -191,7 +191,7 @@ def run_ours(args, rank, world, dev):
     else:
         # Sequence-sharded: this rank's share of the prefix pages; the last rank
         # also holds the tree's pages and applies the tree bitmask.
-        verifier = sh.SequenceShardedVerify()
+        verifier = sh.SequenceShardedVerify(peer_mode=args.peer_mode)
         n_pages_prefix = p0.prefix_len // page
         lo, hi = sh.shard_bounds(n_pages_prefix, world, rank)
         shards = []
@@ -209,7 +209,7 @@ def run_ours(args, rank, world, dev):
         launches_per_step = 2
         workload = (f"config2 sequence-sharded over {world} GPUs: S=65536 paged, 64-node depth-8 tree, 1 layer, "
                     f"bf16, partials exchanged over NVLink as step-tagged words "
-                    f"({'pushed to every peer' if world < 4 else 'merged by each row block owner'}) "
+                    f"({'pushed to every peer' if (args.peer_mode == 'push' or (args.peer_mode == 'auto' and world < 4)) else 'merged by each row block owner'}) "
                     f"and merged by one fused kernel per step")
 
     for _ in range(args.warmup):
@@ -916,7 +916,10 @@ def run_config5(args, rank, world, dev):
     vis = int(tree.keep.sum())
     flops = batch * (4 * m * h * d * arena + 4 * h * d * vis)
     hbm, _ = peaks()
+    mp = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tpeak = float(mp.get("bf16_tflops_sustained", 1400.0))
     value = alg / (ms * 1e-3) / 1e9
+    tflops = flops / (ms * 1e-3) / 1e12
     return {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
@@ -930,10 +933,12 @@ def run_config5(args, rank, world, dev):
                    "launch": "one CUDA graph per step"},
         "arena_forms_ms": {k: round(v, 4) for k, v in times.items()},
         "zero_copy_equals_physical": same, "per_bundle_vs_single_call_max_abs_diff": round(pb_diff, 6),
-        "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(value / world / hbm, 4), "traffic": None,
-                     "kernel": "attn_tc_kernel + split_combine_kernel (zero-copy arena)",
-                     "tensor_tflops": round(flops / (ms * 1e-3) / 1e12 / world, 1)},
+        # 96 rows x GQA 4 per sequence: 384 flops per byte, past the ridge -> tensor-bound
+        "roofline": {"bound": "tensor", "achieved": round(tflops / world, 1), "peak": tpeak, "unit": "TFLOP/s",
+                     "frac": round(tflops / world / tpeak, 4),
+                     "peak_kind": "measured bf16_tflops_sustained (MEASURED_PEAKS.json)" if mp else "fallback",
+                     "hbm_achieved_gbs": round(value / world, 1), "hbm_frac": round(value / world / hbm, 4),
+                     "traffic": None, "kernel": "attn_tc_kernel + split_combine_kernel (zero-copy arena)"},
         "gpu_launches": args.steps * (per_rank + 4),
     }
 
@@ -1360,6 +1365,8 @@ def main():
     ap.add_argument("--nodes", type=int, default=64, help="verify workload: tree nodes (config 2: 64)")
     ap.add_argument("--per-depth", type=int, default=8, help="verify workload: nodes per depth (config 2: 8)")
     ap.add_argument("--root", action="store_true", help="verify workload: prepend the root row (M = nodes + 1)")
+    ap.add_argument("--peer-mode", choices=["auto", "push", "owner"], default="auto",
+                    help="N > 1 verify workload: NVLink exchange mode (auto: push below 4 ranks, owner from 4)")
     ap.add_argument("--workload", choices=["verify", "config3", "config4", "config5", "rope-append", "lmhead-accept", "tree-finalize",
                                            "chunk-retrieve"], default="verify")
     args = ap.parse_args()

@@ -33,16 +33,28 @@ __global__ void __launch_bounds__(256) pack_mask_kernel(int kind, const void* sr
   }
 }
 
-// One thread per (batch, word): AND of the word over all rows.
-__global__ void __launch_bounds__(128) mask_word_summary_kernel(const uint64_t* bits, int rows, int words, int64_t sb,
+// 32 words per block; each word's rows are ANDed by 8 threads (rows g,
+// g + 8, ...), whose results meet in shared memory: the loads of a column are
+// in flight together instead of one after another.
+__global__ void __launch_bounds__(256) mask_word_summary_kernel(const uint64_t* bits, int rows, int words, int64_t sb,
                                                                 int64_t sr, uint8_t* out, int64_t out_sb) {
+  __shared__ uint64_t part[8][32];
   const int b = blockIdx.y;
-  const int w = blockIdx.x * 128 + threadIdx.x;
-  if (w >= words) return;
-  const uint64_t* col = bits + (int64_t)b * sb + w;
+  const int lane = threadIdx.x & 31;
+  const int g = threadIdx.x >> 5;
+  const int w = blockIdx.x * 32 + lane;
   uint64_t acc = ~0ull;
-  for (int r = 0; r < rows && acc == ~0ull; ++r) acc &= col[(int64_t)r * sr];
-  out[(int64_t)b * out_sb + w] = acc == ~0ull ? 1 : 0;
+  if (w < words) {
+    const uint64_t* col = bits + (int64_t)b * sb + w;
+    for (int r = g; r < rows; r += 8) acc &= col[(int64_t)r * sr];
+  }
+  part[g][lane] = acc;
+  __syncthreads();
+  if (g == 0 && w < words) {
+#pragma unroll
+    for (int k = 1; k < 8; ++k) acc &= part[k][lane];
+    out[(int64_t)b * out_sb + w] = acc == ~0ull ? 1 : 0;
+  }
 }
 
 }  // namespace
@@ -58,8 +70,8 @@ extern "C" int tv_mask_word_summary(const uint64_t* bits, int32_t batch, int32_t
   if (sr < words || (batch > 1 && (sb < sr * rows || out_sb < words))) return TV_ERR_SHAPE;
   if (batch > 65535) return TV_ERR_SHAPE;
   if ((reinterpret_cast<uintptr_t>(bits) & 7) != 0) return TV_ERR_ALIGN;
-  dim3 grid((words + 127) / 128, batch);
-  mask_word_summary_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(bits, rows, words, sb, sr, out,
+  dim3 grid((words + 31) / 32, batch);
+  mask_word_summary_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(bits, rows, words, sb, sr, out,
                                                                                out_sb);
   return check_launch();
 }

@@ -24,8 +24,9 @@
 // all zero before the first step.
 //
 // Step e (1, 2, ...) uses slot e & 1.  Each block takes row blocks of RPB rows
-// and combines this rank's split partials of those rows (local memory).  Two
-// exchange modes:
+// and combines this rank's split partials of those rows (local memory),
+// keeping the result in its own rank's region of its own buffer (only this
+// rank writes there).  Two exchange modes:
 //  * push to all (default below 4 ranks): the block stores its rows into
 //    every peer's slot region for this rank, then waits on its own buffer
 //    until every peer's words of the same rows carry step e, and merges all
@@ -202,62 +203,21 @@ __global__ void __launch_bounds__(kThreads, blocks_per_sm(W))
   auto fin_l = [&](char* base, int64_t row) {
     return reinterpret_cast<u64*>(base + slot_off + L.fin_lse_off) + row;
   };
+  // Three phases over this block's row blocks, so the NVLink round trips of
+  // its row blocks overlap instead of running one after another:
+  //   A  combine this rank's split partials of each row, keep the result in
+  //      this rank's own region of its buffer, push it to the peers (push
+  //      mode) or to the row block's owner (owner mode);
+  //   B  for each row this rank merges (all rows in push mode, its own row
+  //      blocks in owner mode): wait for the peers' words, merge in rank
+  //      order, store the outputs (owner mode: and push the final rows);
+  //   C  owner mode, row blocks of other ranks: wait for the final rows.
   bool all_ok = true;
-  for (int rb = blockIdx.x; rb < L.nrb; rb += gridDim.x) {
-    const int64_t row = (int64_t)rb * RPB + threadIdx.x / TPR;
-    if (row >= L.rows) continue;
-    const int owner = OWNED ? (int)((int64_t)rb * W / L.nrb) : rank;
+  auto row_of = [&](int rb) { return (int64_t)rb * RPB + threadIdx.x / TPR; };
+  auto owner_of = [&](int rb) { return OWNED ? (int)((int64_t)rb * W / L.nrb) : rank; };
+  auto store_row = [&](int64_t row, const float4& o, float lse) {
     const int bh = (int)(row / p.R);
     const int r = (int)(row - (int64_t)bh * p.R);
-    float4 own;
-    float own_l;
-    combine_split_row<D>(p, bh, r, q, own, own_l);
-#pragma unroll
-    for (int pr = 0; pr < W; ++pr) {
-      if (pr == rank || (OWNED && pr != owner)) continue;
-      ll_put4(part_o(pb.base[pr], rank, row), own, e);
-      if (q == 0) ll_put1(part_l(pb.base[pr], rank, row), own_l, e);
-    }
-    bool ok = true;
-    float4 o;
-    float lse;
-    if (owner == rank) {
-      float l[W];
-      float4 v[W];
-#pragma unroll
-      for (int pr = 0; pr < W; ++pr) {
-        if (pr == rank) {
-          l[pr] = own_l;
-          v[pr] = own;
-        } else {
-          ok = ll_get4(part_o(mine, pr, row), e, deadline, v[pr]) && ok;
-          ok = ll_get1(part_l(mine, pr, row), e, deadline, l[pr]) && ok;
-        }
-      }
-      merge_ranks<W>(l, v, o, lse);
-      if (!ok) {
-        o = make_float4(nan, nan, nan, nan);
-        lse = nan;
-      }
-      if (OWNED) {
-        // Hand the final rows to every other rank.
-#pragma unroll
-        for (int pr = 0; pr < W; ++pr) {
-          if (pr == rank) continue;
-          ll_put4(fin_o(pb.base[pr], row), o, e);
-          if (q == 0) ll_put1(fin_l(pb.base[pr], row), lse, e);
-        }
-      }
-    } else {
-      // Owner mode, a row block of another rank: its final rows.
-      ok = ll_get4(fin_o(mine, row), e, deadline, o);
-      ok = ll_get1(fin_l(mine, row), e, deadline, lse) && ok;
-      if (!ok) {
-        o = make_float4(nan, nan, nan, nan);
-        lse = nan;
-      }
-    }
-    all_ok = all_ok && ok;
     const int b = bh / p.Hkv;
     const int hk = bh - b * p.Hkv;
     int m, h;
@@ -265,6 +225,69 @@ __global__ void __launch_bounds__(kThreads, blocks_per_sm(W))
     store_out_pair<T>(p, b, m, h, 4 * q, o.x, o.y);
     store_out_pair<T>(p, b, m, h, 4 * q + 2, o.z, o.w);
     if (q == 0) store_row_stats<T>(p, b, m, h, lse);
+  };
+  for (int rb = blockIdx.x; rb < L.nrb; rb += gridDim.x) {           // A
+    const int64_t row = row_of(rb);
+    if (row >= L.rows) continue;
+    const int owner = owner_of(rb);
+    const int bh = (int)(row / p.R);
+    float4 own;
+    float own_l;
+    combine_split_row<D>(p, bh, (int)(row - (int64_t)bh * p.R), q, own, own_l);
+    ll_put4(part_o(mine, rank, row), own, e);
+    if (q == 0) ll_put1(part_l(mine, rank, row), own_l, e);
+#pragma unroll
+    for (int pr = 0; pr < W; ++pr) {
+      if (pr == rank || (OWNED && pr != owner)) continue;
+      ll_put4(part_o(pb.base[pr], rank, row), own, e);
+      if (q == 0) ll_put1(part_l(pb.base[pr], rank, row), own_l, e);
+    }
+  }
+  for (int rb = blockIdx.x; rb < L.nrb; rb += gridDim.x) {           // B
+    const int64_t row = row_of(rb);
+    if (row >= L.rows || owner_of(rb) != rank) continue;
+    bool ok = true;
+    float l[W];
+    float4 v[W];
+#pragma unroll
+    for (int pr = 0; pr < W; ++pr) {
+      ok = ll_get4(part_o(mine, pr, row), e, deadline, v[pr]) && ok;   // own words: already there
+      ok = ll_get1(part_l(mine, pr, row), e, deadline, l[pr]) && ok;
+    }
+    float4 o;
+    float lse;
+    merge_ranks<W>(l, v, o, lse);
+    if (!ok) {
+      o = make_float4(nan, nan, nan, nan);
+      lse = nan;
+    }
+    if (OWNED) {
+      // Hand the final rows to every other rank.
+#pragma unroll
+      for (int pr = 0; pr < W; ++pr) {
+        if (pr == rank) continue;
+        ll_put4(fin_o(pb.base[pr], row), o, e);
+        if (q == 0) ll_put1(fin_l(pb.base[pr], row), lse, e);
+      }
+    }
+    all_ok = all_ok && ok;
+    store_row(row, o, lse);
+  }
+  if (OWNED) {
+    for (int rb = blockIdx.x; rb < L.nrb; rb += gridDim.x) {         // C
+      const int64_t row = row_of(rb);
+      if (row >= L.rows || owner_of(rb) == rank) continue;
+      float4 o;
+      float lse;
+      bool ok = ll_get4(fin_o(mine, row), e, deadline, o);
+      ok = ll_get1(fin_l(mine, row), e, deadline, lse) && ok;
+      if (!ok) {
+        o = make_float4(nan, nan, nan, nan);
+        lse = nan;
+      }
+      all_ok = all_ok && ok;
+      store_row(row, o, lse);
+    }
   }
   if (!all_ok && p.err) atomicExch(p.err, 8);
   __syncthreads();   // every thread has read this block's step count

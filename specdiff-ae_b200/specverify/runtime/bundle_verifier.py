@@ -41,10 +41,13 @@ class FusedBundleVerifier:
         self.prefix_reuse_count = 0
 
     def _bundle_mask(self, masks: List[torch.Tensor], b: int) -> torch.Tensor:
+        """masks[0] for every sequence of the batch (``bundle_verifier.py:196-205``):
+        a [M, N] mask stays one [1, M, N] mask (packed once, read with batch
+        stride 0 by the kernel); a per-sequence [B, M, N] mask is kept."""
         mask = masks[0]
         if mask.dim() == 2:
             mask = mask.unsqueeze(0)
-        return mask.expand(b, -1, -1) if mask.shape[0] < b else mask
+        return mask if mask.shape[0] in (1, b) else mask.expand(b, -1, -1)
 
     def verify_bundle(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, masks: List[torch.Tensor],
                       shared_prefix_len: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
