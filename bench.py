@@ -376,6 +376,9 @@ def run_ours(args, rank, world, dev):
             # The same pipeline without the graph: every step pays the public
             # API's host cost (argument packing, checks, tensor-map encoding,
             # launches) the way an eager serving loop does.
+            e2e_steps(0, args.warmup, held)      # untimed: the eager path's own warm-up after the graph
+            torch.cuda.synchronize()
+            held.clear()
             if world > 1:
                 torch.distributed.barrier()
             torch.cuda.synchronize()

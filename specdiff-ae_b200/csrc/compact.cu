@@ -118,7 +118,27 @@ __global__ void __launch_bounds__(CT) arena_gather_kernel(int heads, const uint6
   const uint8_t* s = reinterpret_cast<const uint8_t*>(kv ? src_v[layer] : src_k[layer]) + head * src_head_stride;
   uint8_t* d = arena + layer * layer_stride + kv * kv_stride + head * head_stride + (int64_t)slot * chunk * row_bytes;
   const int per_row = row_bytes / (int)sizeof(U);
-  const int64_t total = (r1 - r0) * per_row;
+  const int64_t rows = r1 - r0;
+  if (per_row <= CT && CT % per_row == 0) {
+    // A thread keeps one column of the row and walks the rows CT / per_row
+    // apart, four loads in flight before their stores (no 64-bit divisions).
+    const int64_t col = (int64_t)(threadIdx.x % per_row) * sizeof(U);
+    const int rstep = CT / per_row;
+    const uint8_t* sc = s + r0 * src_row_stride + col;
+    uint8_t* dc = d + col;
+    int64_t r = threadIdx.x / per_row;
+    for (; r + 3 * rstep < rows; r += 4 * rstep) {
+      U v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = *reinterpret_cast<const U*>(sc + (r + k * rstep) * src_row_stride);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) *reinterpret_cast<U*>(dc + (r + k * rstep) * row_bytes) = v[k];
+    }
+    for (; r < rows; r += rstep)
+      *reinterpret_cast<U*>(dc + r * row_bytes) = *reinterpret_cast<const U*>(sc + r * src_row_stride);
+    return;
+  }
+  const int64_t total = rows * per_row;
   for (int64_t e = threadIdx.x; e < total; e += CT) {
     const int64_t r = e / per_row;
     const int64_t o = (e - r * per_row) * sizeof(U);
