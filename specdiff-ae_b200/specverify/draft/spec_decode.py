@@ -165,7 +165,9 @@ class SpecDecodeModel:
         # the draft reads the step's start position from the device, so its
         # whole tree growth can be replayed as one CUDA graph per step
         self._start = torch.zeros((), dtype=torch.int64, device=device)
-        self._graphs: Dict[tuple, tuple] = {}
+        self._graphs: Dict[tuple, object] = {}
+        # verify through per-layer-boundary CUDA graphs (verify_graphed)
+        self.graph_verify = True
 
     @classmethod
     def from_config(cls, shape: Optional[LlamaShape] = None, *, device="cuda", dtype=torch.bfloat16, seed: int = 0,
@@ -198,6 +200,95 @@ class SpecDecodeModel:
             if li in s.feature_layers:
                 feats.append(x)
         return rms_norm(x, self.norm, s.rms_eps), torch.cat(feats, dim=-1)
+
+    def verify_graphed(self, ids: torch.Tensor, pos: torch.Tensor, bits: torch.Tensor, start: int):
+        """:meth:`verify` with the torch work between two attention calls (the
+        output projection, the MLP, the next layer's norm and q / k / v
+        projection) replayed from CUDA graphs, one per layer boundary,
+        captured on first use per row count.  RoPE + KV append and the
+        attention, whose arguments change every step (the cache length), are
+        launched between the replays.  Returns static buffers, overwritten by
+        the next call: the final normalised hidden [M, H] and the feature
+        layers' hidden states [M, 3 H]."""
+        t = ids.numel()
+        key = ("verify", t, bits.shape[-1])
+        if key not in self._graphs:
+            self._graphs[key] = self._capture_verify(t, bits.shape[-1])
+        vs = self._graphs[key]
+        vs["ids"].copy_(ids)
+        vs["pos"].copy_(pos)
+        vs["bits"].copy_(bits)
+        vs["graphs"][0].replay()
+        for li in range(self.shape.layers):
+            self._verify_attend(vs, li, start, t)
+            vs["graphs"][li + 1].replay()
+        return vs["hidden"], vs["feats"]
+
+    def _verify_segment(self, vs, li: int):
+        """The torch work after layer li's attention (li = -1: the embedding)
+        up to layer li + 1's q / k / v projection (or the final norm)."""
+        s = self.shape
+        x = vs["x"]
+        if li < 0:
+            torch.index_select(self.embed, 0, vs["ids"], out=x)
+        else:
+            L = self.layers[li]
+            x.add_(vs["o"].view(x.shape[0], -1) @ L.wo.t())
+            gu = rms_norm(x, L.ln2, s.rms_eps) @ L.wgu.t()
+            g, u = gu[:, : s.ffn], gu[:, s.ffn:]
+            x.add_((torch.nn.functional.silu(g) * u) @ L.wdown.t())
+            if li in s.feature_layers:
+                j = s.feature_layers.index(li)
+                vs["feats"][:, j * s.hidden:(j + 1) * s.hidden].copy_(x)
+        if li + 1 < s.layers:
+            L = self.layers[li + 1]
+            torch.matmul(rms_norm(x, L.ln1, s.rms_eps), L.wqkv.t(), out=vs["qkv"])
+        else:
+            vs["hidden"].copy_(rms_norm(x, self.norm, s.rms_eps))
+
+    def _verify_attend(self, vs, li: int, start: int, t: int):
+        """Layer li's RoPE + KV append and verify attention on the static buffers."""
+        s = self.shape
+        hq, hk, d = s.heads, s.kv_heads, s.head_dim
+        qkv = vs["qkv"]
+        q = qkv[:, : hq * d].view(1, t, hq, d).transpose(1, 2)
+        k = qkv[:, hq * d: (hq + hk) * d].view(1, t, hk, d).transpose(1, 2)
+        v = qkv[:, (hq + hk) * d:].view(1, t, hk, d).transpose(1, 2)
+        pk, pv = self.pool[li, 0], self.pool[li, 1]
+        rope_append(q, k, v, self.cos, self.sin, vs["pos"].view(1, t), pk, pv, start=start,
+                    page_table=self.page_table, page_size=self.page, out=vs["qr"], validate=False)
+        attention(vs["qr"].transpose(1, 2), pk, pv, num_keys=start + t, page_table=self.page_table,
+                  mask_bits=vs["bits"][None], mask_len=t, out=vs["o"])
+
+    def _capture_verify(self, t: int, words: int):
+        s = self.shape
+        dev, dt = self.device, self.dtype
+        qkv_dim = (s.heads + 2 * s.kv_heads) * s.head_dim
+        vs = {"ids": torch.zeros(t, dtype=torch.int64, device=dev),
+              "pos": torch.zeros(t, dtype=torch.int64, device=dev),
+              "bits": torch.zeros((t, words), dtype=torch.int64, device=dev),
+              "x": torch.zeros((t, s.hidden), dtype=dt, device=dev),
+              "qkv": torch.zeros((t, qkv_dim), dtype=dt, device=dev),
+              "qr": torch.zeros((1, s.heads, t, s.head_dim), dtype=dt, device=dev),
+              "o": torch.zeros((1, t, s.heads, s.head_dim), dtype=dt, device=dev),
+              "hidden": torch.zeros((t, s.hidden), dtype=dt, device=dev),
+              "feats": torch.zeros((t, len(s.feature_layers) * s.hidden), dtype=dt, device=dev)}
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for li in range(-1, s.layers):
+                self._verify_segment(vs, li)           # warm-up outside the capture
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graphs = []
+        for li in range(-1, s.layers):
+            g = torch.cuda.CUDAGraph()
+            # replayed in capture order, never concurrently: one memory pool
+            with torch.cuda.graph(g, pool=graphs[0].pool() if graphs else None):
+                self._verify_segment(vs, li)
+            graphs.append(g)
+        vs["graphs"] = graphs
+        return vs
 
     # ---- draft --------------------------------------------------------------
     def draft_tree(self, root: torch.Tensor, root_feat: torch.Tensor, width: int, depth: int):
@@ -265,7 +356,10 @@ class SpecDecodeModel:
         pos = torch.cat([torch.full((1,), start, dtype=torch.int64, device=self.device),
                          start + tree["position_ids"]])
         parent = tree["parent_last"]
-        hidden, feats = self.verify(ids, pos, tree["mask_bits"], start)
+        if self.graph_verify:
+            hidden, feats = self.verify_graphed(ids, pos, tree["mask_bits"], start)
+        else:
+            hidden, feats = self.verify(ids, pos, tree["mask_bits"], start)
         ev[2].record()
         acc = accept_from_hidden(hidden, self.lm_head, ids, parent, pos,
                                  depth, mode="sample" if temperature > 0 else "greedy", temperature=temperature,

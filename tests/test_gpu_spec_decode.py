@@ -72,3 +72,26 @@ def test_chain_of_the_true_continuation_is_fully_accepted_and_compacted():
     # the compacted cache continues the same greedy sequence
     rest = _plain_greedy(m, want[depth], PROMPT + depth + 1, 12 - depth - 1)
     assert rest == want[depth + 1:12]
+
+
+def test_graphed_verify_equals_eager_verify():
+    """The verify step replayed from per-layer-boundary CUDA graphs computes
+    what the eager forward does, on the same cache state, for two successive
+    steps (the second reuses the captured graphs at another cache length)."""
+    from specverify.runtime import pack_tree_mask
+    m = _model()
+    m.fill_context(PROMPT, seed=6)
+    t = 9
+    keep = torch.tril(torch.ones(t, t, dtype=torch.int8, device="cuda"))
+    bits = pack_tree_mask(keep)[0]                      # [M, words]
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for start in (PROMPT, PROMPT + 5):
+        ids = torch.randint(0, m.shape.vocab, (t,), device="cuda", generator=g)
+        pos = start + torch.arange(t, device="cuda")
+        h_e, f_e = m.verify(ids, pos, bits, start)
+        h_e, f_e = h_e.clone(), f_e.clone()
+        h_g, f_g = m.verify_graphed(ids, pos, bits, start)
+        torch.cuda.synchronize()
+        assert torch.allclose(h_g.float(), h_e.float(), atol=1e-2, rtol=1e-2)
+        assert torch.allclose(f_g.float(), f_e.float(), atol=1e-2, rtol=1e-2)
+        assert (h_g != h_e).float().mean().item() < 1e-3
