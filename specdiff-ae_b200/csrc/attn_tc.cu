@@ -186,22 +186,23 @@ __device__ __forceinline__ void apply_keep(uint32_t* v, const uint32_t* keep) {
     if (!((keep[j >> 5] >> (j & 31)) & 1u)) v[j] = 0xff800000u;
 }
 
-// Maximum over 64 scores; eight independent chains keep the dependent path
-// short.
+// Maximum over 64 scores: three-input maxima (two scores per instruction)
+// over eight independent chains, which keep the dependent path short.
 __device__ __forceinline__ float chunk_max(const uint32_t* v) {
   float mx[8];
 #pragma unroll
-  for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
+  for (int a = 0; a < 8; ++a) mx[a] = __uint_as_float(v[a]);
 #pragma unroll
-  for (int j = 0; j < 64; ++j) mx[j & 7] = fmaxf(mx[j & 7], __uint_as_float(v[j]));
-  return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+  for (int j = 8; j < 64; j += 2) mx[(j >> 1) & 7] = max3(mx[(j >> 1) & 7], __uint_as_float(v[j]), __uint_as_float(v[j + 1]));
+  return max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
 }
 
 // P = exp2(s * sl2 - mu) for 64 scores, packed as 16-bit pairs (key 2k in the
-// low half of word k: the layout the PV MMA reads A from); returns sum of P.
+// low half of word k: the layout the PV MMA reads A from); returns sum of P,
+// accumulated as packed pairs (one add per two keys).
 template <typename T>
 __device__ __forceinline__ float chunk_exp(const uint32_t* v, float sl2, float mu, uint32_t* pk) {
-  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 s[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
   for (int j = 0; j < 64; j += 2) {
     // scale and shift two scores with one packed f32x2 FMA
@@ -209,10 +210,10 @@ __device__ __forceinline__ float chunk_exp(const uint32_t* v, float sl2, float m
                           make_float2(-mu, -mu));
     const float p0 = fast_exp2(x.x);
     const float p1 = fast_exp2(x.y);
-    s[(j >> 1) & 3] += p0 + p1;
+    s[(j >> 1) & 1] = add2(s[(j >> 1) & 1], make_float2(p0, p1));
     pk[j >> 1] = pack_pair<T>(p0, p1);
   }
-  return (s[0] + s[1]) + (s[2] + s[3]);
+  return (s[0].x + s[1].x) + (s[0].y + s[1].y);
 }
 
 template <typename T, bool PAGED, bool WIDE>

@@ -183,6 +183,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
 }
 
 // ---- packed fp32 pairs (sm_100 f32x2 arithmetic) --------------------------------
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// Three-input maximum (sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   float2 d;
   asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
