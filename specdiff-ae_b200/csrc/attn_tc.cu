@@ -98,11 +98,16 @@ struct Bars {
   uint64_t pv_done[PBUF];   // per P buffer: PV of the tile in it retired
   uint64_t o_done;
   uint64_t pair[4];         // per TMEM lane quarter: the two softmax warps meet at the end
-  uint64_t ref_bar[4];      // per quarter: one phase per tile, the reference max is published
   uint32_t tmem;
   int abort;
-  float mref[ROWS];         // reference max (log2 units) after the latest decided tile
-  float xm[2 * ROWS];       // final references and partial sums of the two warps of a row
+  // Per row, the reference max (log2 units) after the latest decided tile in
+  // the low half and that tile's index + 1 in the high half of one word: a
+  // reader polls its row's word until the tile it needs is there.  At the
+  // end the same bytes carry the two warps' final references (xm).
+  union {
+    uint64_t mref[ROWS];
+    float xm[2 * ROWS];     // final references and partial sums of the two warps of a row
+  };
   float xl[2 * ROWS];
 };
 static_assert(sizeof(Bars) <= 3072, "barrier block");
@@ -175,6 +180,30 @@ __device__ __forceinline__ uint32_t keep_bits(const uint64_t* mrow, int rel0, in
     k |= got << (a - rel0);
   }
   return k;
+}
+
+// The reference hand-off word of a row: value bits low, tile index + 1 high;
+// one aligned 64-bit shared-memory access is single-copy atomic.
+__device__ __forceinline__ void ref_put(uint64_t* w, float v, uint32_t tag) {
+  const uint64_t x = ((uint64_t)tag << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.shared.u64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(w)), "l"(x) : "memory");
+}
+// Polls until the word carries `tag` (bounded like mbar_wait).
+__device__ __forceinline__ bool ref_wait(const uint64_t* w, uint32_t tag, volatile int* abort, float& v) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(w);
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint64_t x;
+    asm volatile("ld.volatile.shared.u64 %0, [%1];" : "=l"(x) : "r"(a) : "memory");
+    if ((uint32_t)(x >> 32) == tag) {
+      v = __uint_as_float((uint32_t)x);
+      return true;
+    }
+    if ((it & 255u) == 255u) {
+      if (*abort) return false;
+      if (global_ns() - t0 > 2000000000ull) return false;
+    }
+  }
 }
 
 // Scores of keys the row may not see become -inf in place (their P is then
@@ -263,11 +292,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int s = 0; s < PBUF; ++s) mbar_init(&bars->pv_done[s], 1);
     mbar_init(&bars->o_done, 1);
-    for (int q = 0; q < 4; ++q) {
-      mbar_init(&bars->pair[q], 64);
-      mbar_init(&bars->ref_bar[q], 1);
-    }
+    for (int q = 0; q < 4; ++q) mbar_init(&bars->pair[q], 64);
     bars->abort = 0;
+    for (int r = 0; r < ROWS; ++r) bars->mref[r] = 0ull;
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -280,10 +307,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     tmem_relinquish();
   }
 
+  // Barriers and the tensor-memory address are visible after this; the
+  // producers start their loads at once, while the other ten warps stage the
+  // queries (only the S issuer reads them, after the named barrier below).
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+
   // ---- queries -> shared memory, 128-byte swizzled [d-half][row][64] --------
-  {
+  if (warp != 0 && warp != 10) {
+    constexpr int QT = THREADS - 64;                       // staging threads
+    const int lid = threadIdx.x - (warp < 10 ? 32 : 64);
     const T* qb = static_cast<const T*>(p.q);
-    for (int idx = threadIdx.x; idx < ROWS * 16; idx += THREADS) {
+    for (int idx = lid; idx < ROWS * 16; idx += QT) {
       const int row = idx >> 4;
       const int c = idx & 15;
       const int r = rb * ROWS + row;
@@ -297,12 +334,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int dh = c >> 3, cc = c & 7;
       *reinterpret_cast<uint4*>(sQ + dh * SUB + row * 128 + ((cc ^ (row & 7)) << 4)) = val;
     }
+    fence_proxy_async();
+    asm volatile("bar.sync 1, %0;" ::"n"(QT) : "memory");
   }
-  fence_proxy_async();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = bars->tmem;
 
   if (warp == 0 || warp == 10) {
     // ---------------------------------------------------------------- producers
@@ -484,7 +518,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // work on successive tiles at the same time.  Warp w covers TMEM lane
     // quarter w % 4: each thread owns one query row and all 128 keys of its
     // tiles.  The running reference max passes from tile to tile through
-    // shared memory (one mbarrier phase per tile and quarter); it only moves
+    // shared memory (one tagged word per row, polled by the next tile's
+    // thread of the same row); it only moves
     // when a tile's max exceeds it by more than 2^8, and then O is rescaled
     // before that tile's PV.  Each warp keeps a partial row sum against the
     // reference it last saw; the two are combined at the end.
@@ -499,7 +534,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t o_addr = lane_base + O_COL;
     const float sl2 = p.scale_log2;
     const int mlen = p.mask_len;
-    uint64_t* ref_bar = &bars->ref_bar[q4];
+    uint64_t* ref_word = &bars->mref[rr];
     uint64_t* pair = &bars->pair[q4];             // both warps of the quarter meet once, at the end
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -571,12 +606,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       // Reference after tile i-1 (published by the other warp of the quarter).
       float mprev = -INFINITY;
       if (i > 0) {
-        if (!__all_sync(0xffffffffu, mbar_wait(ref_bar, (i - 1) & 1, abort))) {
+        if (!__all_sync(0xffffffffu, ref_wait(ref_word, (uint32_t)i, abort, mprev))) {
           raise_abort(bars, err, 6);
           ok = false;
           break;
         }
-        mprev = bars->mref[rr];
       }
       if (mprev > m_run) {          // the reference only grows
         l_run *= fast_exp2(m_run - mprev);
@@ -589,9 +623,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         alpha = fast_exp2(m_run - mt);
         m_run = mt;
       }
-      bars->mref[rr] = m_run;       // reference for tile i+1
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ref_bar);
+      ref_put(ref_word, m_run, (uint32_t)i + 1u);   // reference for tile i+1
       const bool need_o = bump && i > 0;
       if (__any_sync(0xffffffffu, need_o)) {
         // O holds tiles up to i-1 scaled to mprev; PV(i-1) must retire first.
