@@ -479,8 +479,8 @@ def run_ours(args, rank, world, dev):
             "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6.65 TB/s",
             "traffic": NCU_TRAFFIC_BYTES if world == 1 and TREE == {"nodes": 64, "per_depth": 8, "root": False}
             else None,
-            "kernel": "attn_tc_kernel (the whole call: splits merged in the kernel); traffic is its per launch "
-                      "(ncu)",
+            "kernel": "attn_tc_kernel + split_combine_kernel: achieved is timed over the whole verify call "
+                      "(both launches, CUDA events); traffic is attn_tc_kernel's per launch (ncu)",
             "tensor_tflops": round(flops / (ms * 1e-3) / 1e12 / world, 1),
         },
         "gpu_launches": launches_per_step * args.steps,

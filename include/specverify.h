@@ -500,6 +500,19 @@ int tv_tree_finalize(int32_t nnodes, int32_t depth, int32_t k, const int64_t* to
                      int64_t* position_ids, int64_t* parent_pos, int8_t* mask, uint64_t* mask_bits,
                      int32_t* status, void* stream);
 
+/* ---- decoder-layer elementwise work around the verify path --------------------
+ * tv_rms_norm replaces LlamaRMSNorm.forward (runtime/llama_target_model.py:124-138):
+ *   y[r] = weight * T(x[r] * rsqrt(mean(x[r]^2) + eps)), statistics in fp32,
+ *   the normalised row rounded to T before the weight multiply.
+ * tv_silu_mul replaces act_fn(gate_proj(x)) * up_proj(x) of LlamaMLP.forward
+ *   (:506-538, act_fn = SiLU): out[r] = T(silu(gate[r])) * up[r].
+ * Strides in elements; cols a multiple of 8; pointers 16-byte aligned and
+ * strides multiples of 8 elements (TV_ERR_ALIGN otherwise). */
+int tv_rms_norm(const void* x, int64_t x_row_stride, const void* weight, void* y, int64_t y_row_stride,
+                int32_t rows, int32_t cols, float eps, int32_t dtype, void* stream);
+int tv_silu_mul(const void* gate, const void* up, int64_t in_row_stride, void* out, int64_t out_row_stride,
+                int32_t rows, int32_t cols, int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

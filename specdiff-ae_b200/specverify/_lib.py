@@ -131,6 +131,8 @@ _SIGNATURES = {
     "tv_chunk_select": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp, c_size,
                                 c_vp, c_vp]),
     "tv_gather_rows": (c_i32, [c_i32, c_i32, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_vp]),
+    "tv_rms_norm": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i32, c_i32, c_f32, c_i32, c_vp]),
+    "tv_silu_mul": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_i64, c_i32, c_i32, c_i32, c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

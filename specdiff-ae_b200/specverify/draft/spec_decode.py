@@ -67,9 +67,29 @@ class LlamaShape:
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """``LlamaRMSNorm``: fp32 variance, scaled in the input dtype."""
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+    """``LlamaRMSNorm`` (``llama_target_model.py:124-138``) of the rows of a 2-D
+    ``x``: fp32 statistics, the normalised row rounded to the input dtype
+    before the weight multiply; one launch (``tv_rms_norm``)."""
+    if x.dim() != 2 or x.stride(1) != 1 or w.dim() != 1 or w.stride(0) != 1:
+        raise _lib.SpecVerifyError(-3, "rms_norm needs x [rows, cols] with unit column stride and a 1-D weight")
+    y = torch.empty((x.shape[0], x.shape[1]), dtype=x.dtype, device=x.device)
+    st = _lib.load().tv_rms_norm(x.data_ptr(), x.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), x.shape[0],
+                                 x.shape[1], float(eps), _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device))
+    _lib.check(st, "tv_rms_norm")
+    return y
+
+
+def silu_mul(gu: torch.Tensor, ffn: int) -> torch.Tensor:
+    """``act_fn(gate) * up`` of ``LlamaMLP`` (SiLU, ``llama_target_model.py:506-538``)
+    for the fused ``[rows, 2 ffn]`` gate/up projection; one launch (``tv_silu_mul``)."""
+    if gu.dim() != 2 or gu.stride(1) != 1 or gu.shape[1] != 2 * ffn:
+        raise _lib.SpecVerifyError(-3, "silu_mul needs gu [rows, 2 * ffn] with unit column stride")
+    y = torch.empty((gu.shape[0], ffn), dtype=gu.dtype, device=gu.device)
+    g, u = gu[:, :ffn], gu[:, ffn:]
+    st = _lib.load().tv_silu_mul(g.data_ptr(), u.data_ptr(), gu.stride(0), y.data_ptr(), y.stride(0), gu.shape[0],
+                                 ffn, _lib.dtype_code(gu.dtype), _lib.stream_ptr(gu.device))
+    _lib.check(st, "tv_silu_mul")
+    return y
 
 
 def rope_tables(head_dim: int, max_pos: int, theta: float, device, dtype=torch.bfloat16):
@@ -114,10 +134,9 @@ def _layer_forward(s: LlamaShape, L: _Layer, x_in: torch.Tensor, resid: torch.Te
                            page_size=pool_k.shape[2], validate=False)
     o = attention(qr.transpose(1, 2), pool_k, pool_v, num_keys=start + t, page_table=page_table, mask_bits=bits,
                   mask_len=mask_len)
-    h = resid + o.view(t, hq * d) @ L.wo.t()
+    h = torch.addmm(resid, o.view(t, hq * d), L.wo.t())
     gu = rms_norm(h, L.ln2, s.rms_eps) @ L.wgu.t()
-    g, u = gu[:, : s.ffn], gu[:, s.ffn:]
-    return h + (torch.nn.functional.silu(g) * u) @ L.wdown.t()
+    return torch.addmm(h, silu_mul(gu, s.ffn), L.wdown.t())
 
 
 class SpecDecodeModel:
@@ -233,10 +252,9 @@ class SpecDecodeModel:
             torch.index_select(self.embed, 0, vs["ids"], out=x)
         else:
             L = self.layers[li]
-            x.add_(vs["o"].view(x.shape[0], -1) @ L.wo.t())
+            x.addmm_(vs["o"].view(x.shape[0], -1), L.wo.t())
             gu = rms_norm(x, L.ln2, s.rms_eps) @ L.wgu.t()
-            g, u = gu[:, : s.ffn], gu[:, s.ffn:]
-            x.add_((torch.nn.functional.silu(g) * u) @ L.wdown.t())
+            x.addmm_(silu_mul(gu, s.ffn), L.wdown.t())
             if li in s.feature_layers:
                 j = s.feature_layers.index(li)
                 vs["feats"][:, j * s.hidden:(j + 1) * s.hidden].copy_(x)

@@ -95,3 +95,28 @@ def test_graphed_verify_equals_eager_verify():
         assert torch.allclose(h_g.float(), h_e.float(), atol=1e-2, rtol=1e-2)
         assert torch.allclose(f_g.float(), f_e.float(), atol=1e-2, rtol=1e-2)
         assert (h_g != h_e).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_rms_norm_and_silu_mul_match_the_reference_formulas(dtype):
+    """tv_rms_norm / tv_silu_mul against LlamaRMSNorm and SiLU(gate) * up as
+    the reference writes them in torch: equal up to one rounding of the
+    output type (the fp32 sum of squares is accumulated in another order)."""
+    from specverify.draft.spec_decode import rms_norm, silu_mul
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = (torch.randn(65, 4096, device="cuda", generator=g) * 3).to(dtype)
+    w = (1 + 0.1 * torch.randn(4096, device="cuda", generator=g)).to(dtype)
+    xf = x.float()
+    want = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).to(dtype) * w
+    got = rms_norm(x, w, 1e-5)
+    assert torch.allclose(got.float(), want.float(), rtol=1 / 64, atol=1e-6)
+    assert (got != want).float().mean().item() < 0.01
+    # a row-strided view (every other row) and an offset weight slice
+    w2 = torch.cat([w, w])
+    got2 = rms_norm(x[::2], w2[4096:], 1e-5)
+    assert torch.equal(got2, got[::2])
+    gu = (torch.randn(65, 2 * 1024, device="cuda", generator=g) * 4).to(dtype)
+    want = torch.nn.functional.silu(gu[:, :1024]) * gu[:, 1024:]
+    got = silu_mul(gu, 1024)
+    assert torch.allclose(got.float(), want.float(), rtol=1 / 64, atol=1e-6)
+    assert (got != want).float().mean().item() < 0.001
