@@ -19,7 +19,8 @@
 //   slot s (s = 0, 1) at s * slot_bytes, all 8-byte words:
 //     O   [W][rows][D]      -- rank r's partial at r * rows * D
 //     LSE [W][rows]
-//     final O [rows][D], final LSE [rows]   (owner mode)
+//     final O [rows][D], final LSE [rows]   (owner mode; with a 16-bit
+//         output the final O words carry two values each: [rows][D / 2])
 //   then int32 step counts, one per block of the kernel's grid
 // all zero before the first step.
 //
@@ -34,9 +35,11 @@
 //    fp32 partial leaves each rank.
 //  * owner (default from 4 ranks on): row block rb belongs to rank
 //    rb * W / nrb.  The other ranks push their partial rows of rb to the owner
-//    only; the owner merges them in rank order and pushes the final fp32 rows
-//    to every other rank, which convert them exactly as the owner does.  Two
-//    hops, but about 4 (W - 1) / W partials leave each rank instead of 2 (W - 1).
+//    only; the owner merges them in rank order and pushes the final rows to
+//    every other rank -- in the output type (two 16-bit values per word, or
+//    fp32 words for an fp32 output), so every rank writes what the owner
+//    writes.  Two hops, but about 3 (W - 1) / W partials' worth of words
+//    leave each rank instead of 2 (W - 1).
 // Either way every rank computes bit-identical outputs and no thread waits on
 // more than the rows it is working on.
 //
@@ -149,6 +152,41 @@ __device__ __forceinline__ bool ll_get1(const u64* src, int e, unsigned long lon
   }
 }
 
+// Final rows in the output's 16-bit type (owner mode): a pair of values per
+// word (packed as the output stores them) and the step in the high half, so
+// the hand-back moves half the bytes of fp32 words and the receivers write
+// exactly what the owner writes.
+template <typename T>
+__device__ __forceinline__ void ll_put4h(u64* dst, float4 v, int e) {
+  const u64 a = ((u64)(unsigned)e << 32) | Elem<T>::pack2(v.x, v.y);
+  const u64 b = ((u64)(unsigned)e << 32) | Elem<T>::pack2(v.z, v.w);
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(a), "l"(b) : "memory");
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack_pair(unsigned w) {
+  T lo, hi;
+  const unsigned short wl = (unsigned short)(w & 0xffffu), wh = (unsigned short)(w >> 16);
+  memcpy(&lo, &wl, 2);
+  memcpy(&hi, &wh, 2);
+  return make_float2(Elem<T>::to_f(lo), Elem<T>::to_f(hi));
+}
+template <typename T>
+__device__ __forceinline__ bool ll_get4h(const u64* src, int e, unsigned long long deadline, float4& v) {
+  unsigned it = 0;
+  for (;;) {
+    u64 a, b;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(src) : "memory");
+    const int ta = (int)(a >> 32), tb = (int)(b >> 32);
+    if (ta == e && tb == e) {
+      const float2 x = unpack_pair<T>((unsigned)a), y = unpack_pair<T>((unsigned)b);
+      v = make_float4(x.x, x.y, y.x, y.y);
+      return true;
+    }
+    if (ta > e || tb > e) return false;
+    if ((++it & 63u) == 0 && now_ns() > deadline) return false;
+  }
+}
+
 struct PeerBases {
   char* base[kMaxPeers];
 };
@@ -199,6 +237,9 @@ __global__ void __launch_bounds__(kThreads, blocks_per_sm(W))
   };
   auto fin_o = [&](char* base, int64_t row) {
     return reinterpret_cast<u64*>(base + slot_off + L.fin_off) + row * D + 4 * q;
+  };
+  auto fin_oh = [&](char* base, int64_t row) {      // 16-bit output: two values per word
+    return reinterpret_cast<u64*>(base + slot_off + L.fin_off) + row * (D / 2) + 2 * q;
   };
   auto fin_l = [&](char* base, int64_t row) {
     return reinterpret_cast<u64*>(base + slot_off + L.fin_lse_off) + row;
@@ -266,7 +307,8 @@ __global__ void __launch_bounds__(kThreads, blocks_per_sm(W))
 #pragma unroll
       for (int pr = 0; pr < W; ++pr) {
         if (pr == rank) continue;
-        ll_put4(fin_o(pb.base[pr], row), o, e);
+        if (p.out_f32) ll_put4(fin_o(pb.base[pr], row), o, e);
+        else ll_put4h<T>(fin_oh(pb.base[pr], row), o, e);
         if (q == 0) ll_put1(fin_l(pb.base[pr], row), lse, e);
       }
     }
@@ -279,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, blocks_per_sm(W))
       if (row >= L.rows || owner_of(rb) == rank) continue;
       float4 o;
       float lse;
-      bool ok = ll_get4(fin_o(mine, row), e, deadline, o);
+      bool ok = p.out_f32 ? ll_get4(fin_o(mine, row), e, deadline, o) : ll_get4h<T>(fin_oh(mine, row), e, deadline, o);
       ok = ll_get1(fin_l(mine, row), e, deadline, lse) && ok;
       if (!ok) {
         o = make_float4(nan, nan, nan, nan);

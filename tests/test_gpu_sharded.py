@@ -261,3 +261,55 @@ def test_sharded_entry_lagging_rank_flags_overwritten_words():
     assert int(status.item()) == 8
     assert torch.isnan(out.float()).all() and torch.isnan(lse).all()
     assert elapsed < 1.5, f"the later step should be seen at once, not after the 2 s deadline ({elapsed:.2f} s)"
+
+
+@pytest.mark.skipif(not cuda_ok(), reason="needs CUDA")
+def test_sharded_entry_owner_mode_hands_back_16bit_final_rows():
+    """Owner mode, rank 0 of 2 on one GPU.  The 'peer' has posted, for step 1,
+    its partial of the row blocks rank 0 owns (LSE -inf: nothing to add) and
+    the final rows of the blocks it owns itself (two bf16 values + the step
+    per word, as the reference result's rows).  Rank 0 must then write the
+    one-rank result bit for bit on every row, and hand its own blocks' final
+    rows to the peer in the same 16-bit word format."""
+    from specverify.runtime import attention
+    w, bits = _one_gpu_request(1024, seed=9)
+    b, m, h, d = w.q.shape
+    hkv = w.k_pool.shape[1]
+    g = h // hkv
+    rows = b * m * h
+    ref = torch.empty_like(w.q)
+    ref_lse = torch.empty(w.q.shape[:3], device="cuda")
+    attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table, mask_bits=bits,
+              mask_len=m, out=ref, lse=ref_lse)
+    # the kernel's row order (b, kv head, node, group member)
+    ref_rows = ref.view(b, m, hkv, g, d).permute(0, 2, 1, 3, 4).reshape(rows, d)
+    lse_rows = ref_lse.view(b, m, hkv, g).permute(0, 2, 1, 3).reshape(rows)
+    rpb = 128 // (d // 4)                                   # rows per row block of the exchange kernel
+    nrb = -(-rows // rpb)
+    own = torch.tensor([(r // rpb) * 2 // nrb == 0 for r in range(rows)], device="cuda")
+    a = lambda x: (x + 255) & ~255
+    L = _slot_layout(2, rows, d)
+    slot = L["slot"]                                         # step 1 uses slot 1
+    fin = slot + a(2 * rows * d * 8) + a(2 * rows * 8)
+    fin_lse = fin + a(rows * d * 8)
+    mine = _exchange_buffer(2, rows, d)
+    peer = _exchange_buffer(2, rows, d)
+    tag = 1 << 32
+    words = mine.view(torch.int64)
+    o1 = slot // 8 + rows * d                                # rank 1's partial region
+    words[o1:o1 + rows * d] = tag
+    l1 = (slot + L["lse"]) // 8 + rows
+    words[l1:l1 + rows] = tag | 0xFF800000
+    pairs = ref_rows.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF   # [rows, d / 2]
+    fw = words[fin // 8:fin // 8 + rows * d // 2].view(rows, d // 2)
+    fw[~own] = (pairs | tag)[~own]
+    lw = words[fin_lse // 8:fin_lse // 8 + rows]
+    lse_bits = lse_rows.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    lw[~own] = (lse_bits | tag)[~own]
+    out, lse = _sharded_call(w, bits, [mine.data_ptr(), peer.data_ptr()], 2, 0, kernel=32)
+    assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
+    pw = peer.view(torch.int64)
+    got = pw[fin // 8:fin // 8 + rows * d // 2].view(rows, d // 2)
+    assert torch.equal(got[own], (pairs | tag)[own])
+    got_l = pw[fin_lse // 8:fin_lse // 8 + rows]
+    assert torch.equal(got_l[own], (lse_bits | tag)[own])
