@@ -441,6 +441,7 @@ def run_ours(args, rank, world, dev):
             "what": "repeat_kv of the contiguous cache + prefix attention with LSE + masked tree attention with "
                     "the sigmoid merge weight + in-place merge (llama_target_model.py:793-864) on the same GPU"}
         torch.cuda.empty_cache()
+        extra["acceptance"] = acceptance_bar(dev, args.steps, args.warmup)
 
     graphs.clear()   # graphs holding NCCL work are released before the process group goes
     total_bytes = alg_bytes  # whole job: the full 64K problem once per step (sharded or not)
@@ -598,6 +599,46 @@ def reference_gpu_bar(probs, steps, warmup):
 # ---------------------------------------------------------------------------
 # reference CPU path (oracle restatement)
 # ---------------------------------------------------------------------------
+
+def acceptance_bar(dev, steps: int, warmup: int):
+    """Greedy acceptance at BASELINE config 1's shape (65 tree rows over the
+    128256-word vocabulary, seed 0): the device kernels through the public
+    API (``specverify.draft.accept``, CUDA events, logits already on the
+    device), and the reference's ``verify_new`` greedy restated on the host
+    (the oracle: argmax rows, closure along parents, best path) timed on the
+    same logits -- BASELINE's CPU acceptance row."""
+    from oracle import acceptance as oacc
+    from specverify import workloads as wl
+    from specverify.draft import accept
+    c = wl.config1(seed=0)
+    logits, draft = c.logits.to(dev), c.draft.to(dev)
+    parent, pos = c.tree.parent.to(dev), c.positions.to(dev)
+    for _ in range(warmup):
+        accept(logits, draft, parent, pos, 8)
+    torch.cuda.synchronize()
+    n = max(steps, 10)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        acc = accept(logits, draft, parent, pos, 8)
+    e1.record()
+    torch.cuda.synchronize()
+    gpu_ms = e0.elapsed_time(e1) / n
+    got = acc.to_host()
+    ln, dn, pn, qn = c.logits.numpy(), c.draft.numpy(), c.tree.parent.numpy(), c.positions.numpy()
+    oacc.accept_greedy(ln, dn, pn, qn, 8)
+    best = float("inf")
+    for _ in range(3):
+        t0 = time.perf_counter()
+        ref = oacc.accept_greedy(ln, dn, pn, qn, 8)
+        best = min(best, time.perf_counter() - t0)
+    return {"rows": int(c.logits.shape[-2]), "vocab": int(c.logits.shape[-1]),
+            "gpu_ms_per_call": round(gpu_ms, 4), "cpu_ms_per_call": round(best * 1e3, 3), "cpu_cores": 1,
+            "same_path": got["path"] == ref["path"] and got["accept_length"] == ref["accept_length"],
+            "what": "greedy acceptance (argmax over the vocabulary, closure along parents, best path): "
+                    "device kernels eagerly through specverify.draft.accept vs the reference's verify_new "
+                    "greedy restated on the host (numpy, one core)"}
+
 
 def cpu_reference_setup(prefix: int = 65536, seed: int = 0):
     """The reference's CPU verify pipeline (fp32, repeat_kv-expanded, pages
