@@ -227,3 +227,29 @@ def test_config2_with_root_row_and_poisoned_last_page(prefix_len):
     ref, ref_lse = _oracle_by_kv_head(w.q.cpu(), k.cpu(), v.cpu(), w.tree.keep, w.prefix_len)
     _close(out, ref)
     _close(lse, ref_lse, atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("prefix_len", [16384, 131072 // 8 * 3])
+def test_128_node_tree_balanced_split_plan_against_oracle(prefix_len):
+    """128 nodes x GQA 4 = 512 rows per KV head (config 4's tree): 32
+    row-block CTAs per split, so four equal splits would leave 20 SMs idle
+    and the planner adds a fifth, shorter split (its CTAs fill the idle SMs
+    and then the first SMs freed).  Every row against the oracle, and the
+    result equal (to the split-merge rounding) to a plain four-split plan."""
+    from specverify import workloads as wl
+    from specverify.runtime import verify_attention
+    from specverify.runtime.tree_attention import describe_attention, pack_tree_mask
+    w = wl.paged_verify(seed=12, nodes=128, per_depth=13, prefix_len=prefix_len)
+    bits = pack_tree_mask(w.tree.keep.cuda())
+    plan = describe_attention(w.q, w.k_pool, w.v_pool, num_keys=w.num_keys, page_table=w.page_table,
+                              mask_bits=bits, mask_len=w.tree.rows)
+    assert plan["kernel"] == "tcgen05" and plan["splits"] == 5, plan
+    out, lse = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
+                                return_lse=True)
+    k, v = w.contiguous_kv(0)
+    ref, ref_lse = _oracle_by_kv_head(w.q.cpu(), k.cpu(), v.cpu(), w.tree.keep, w.prefix_len)
+    _close(out, ref)
+    _close(lse, ref_lse, atol=1e-3, rtol=1e-4)
+    four = verify_attention(w.q, w.k_pool, w.v_pool, w.prefix_len, w.tree.keep.cuda(), page_table=w.page_table,
+                            num_splits=4)
+    assert (four.float() - out.float()).abs().max().item() < 2e-3
