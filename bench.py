@@ -632,8 +632,21 @@ def acceptance_bar(dev, steps: int, warmup: int):
         t0 = time.perf_counter()
         ref = oacc.accept_greedy(ln, dn, pn, qn, 8)
         best = min(best, time.perf_counter() - t0)
+    # the reference's CPU verify-attention layer at the same config-1 shapes
+    # (S = 4096 contiguous, 65 rows, fp32, repeat_kv, all host cores)
+    from oracle import attention as oatt
+    torch.set_num_threads(os.cpu_count() or 1)
+    layer = lambda: oatt.reference_verify_layer(c.q_raw, c.k_prefix, c.v_prefix, c.k_tree_raw, c.v_tree,
+                                                c.tree.keep)
+    layer()
+    att = float("inf")
+    for _ in range(3):
+        t0 = time.perf_counter()
+        layer()
+        att = min(att, time.perf_counter() - t0)
     return {"rows": int(c.logits.shape[-2]), "vocab": int(c.logits.shape[-1]),
             "gpu_ms_per_call": round(gpu_ms, 4), "cpu_ms_per_call": round(best * 1e3, 3), "cpu_cores": 1,
+            "cpu_config1_attention_ms": round(att * 1e3, 2), "cpu_config1_attention_cores": torch.get_num_threads(),
             "same_path": got["path"] == ref["path"] and got["accept_length"] == ref["accept_length"],
             "what": "greedy acceptance (argmax over the vocabulary, closure along parents, best path): "
                     "device kernels eagerly through specverify.draft.accept vs the reference's verify_new "
