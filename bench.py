@@ -831,7 +831,8 @@ def run_config4(args, rank, world, dev):
                      "frac": round(tflops / world / tpeak, 4),
                      "peak_kind": "measured bf16_tflops_sustained (MEASURED_PEAKS.json)" if mp else "fallback",
                      "hbm_frac": round(value / world / hbm, 4), "traffic": None,
-                     "kernel": "attn_tc_kernel + sharded_combine_kernel per layer"},
+                     "kernel": "attn_tc_kernel + " + ("split_combine_kernel" if world == 1 else "sharded_combine_kernel")
+                               + " per layer"},
         "gpu_launches": args.steps * layers * 2,
     }
 
